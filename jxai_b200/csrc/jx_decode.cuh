@@ -1,0 +1,536 @@
+// jx_decode.cuh -- the fused decode-attention kernel for sm_100a.
+//
+// One launch performs, for every (sequence, layer) pair of a step, the work
+// jxai's forward_token does inline per layer (src/transformer.cpp:2497-2566):
+// RoPE on q and k, the append of k and v at `pos`, and grouped-query attention
+// over every attended cache row.  Design:
+//
+//  * Work space.  Rows are flattened over (pair, kv head, row); each of the P
+//    persistent CTAs takes an equal contiguous slice of that space, so bytes
+//    are balanced across SMs however ragged the sequences are.  A slice cuts
+//    segments (one segment = one (pair, kv head)) into pieces.
+//  * Pipeline.  Warp 4 is the producer: it streams 32-row K and V tiles of the
+//    current piece into a ring of shared-memory stages with 4-D TMA tile loads
+//    (128-byte swizzle, no multicast), completion tracked by mbarriers.
+//    Warps 0-3 are consumers; tile k goes to warp k % 4.
+//  * Math on CUDA cores (the step is HBM-bound: ~2 flop per KV byte at group 4).
+//    QK: lane = cache row, dot product over head_dim in ascending order with
+//    fused multiply-adds (the reference's `dot += q[d]*k[d]` order), q of the
+//    whole query group broadcast from shared memory.  Online softmax per tile
+//    with warp-shuffle max; PV: lane = head dimensions, p broadcast from
+//    shared memory.
+//  * Merge.  At the end of a piece the four warps' (m, l, o) are merged through
+//    shared memory.  A piece that is a whole segment writes the normalised
+//    output directly; otherwise it writes a partial to scratch and the last
+//    CTA to finish the segment (atomic counter, no waiting) merges all of them
+//    by log-sum-exp and resets the counter.
+//  * Append.  The CTA that owns a segment's newest row rotates and stores that
+//    row's k and v slice (producer warp), fences the generic->async proxy, and
+//    only then loads the tile holding it.
+//
+// Template parameters: HD = head_dim, GP = query heads per kv head rounded up
+// to 1/2/4/8, DT = cache element type (DT_F32 / DT_BF16 / DT_F16T).
+#pragma once
+
+#include "jx_device.cuh"
+#include "jx_internal.h"
+
+namespace jx {
+
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kThreads = kConsumerThreads + 32;
+constexpr int kTileRows = 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int HD, int DT>
+struct Geo {
+    static constexpr int ESZ = DT == DT_F32 ? 4 : 2;
+    static constexpr int ROWB = HD * ESZ;                // bytes of one kv-head row
+    static constexpr int BOX = ROWB < 128 ? ROWB : 128;  // TMA box inner extent (bytes)
+    static constexpr int NB = ROWB / BOX;                // boxes per row
+    static constexpr int BOXE = BOX / ESZ;               // box inner extent (elements)
+    static constexpr int TILEB = kTileRows * ROWB;       // one K (or V) tile
+    static constexpr int SWZ = BOX / 16 - 1;             // swizzle row mask
+    static constexpr int EPC = 16 / ESZ;                 // elements per 16-byte chunk
+    static constexpr int CHUNKS = ROWB / 16;             // chunks per row
+    static constexpr int CPB = BOX / 16;                 // chunks per box row
+    static constexpr int DPL = HD / 32;                  // head dims per lane in PV
+    static constexpr int LANEB = DPL * ESZ;              // bytes per lane per V row
+    static_assert(ROWB % 64 == 0, "row bytes must be a multiple of 64");
+};
+
+// Shared-memory carve-up, identical on host and device.
+template <int HD, int GP, int DT>
+struct SmemLayout {
+    using G = Geo<HD, DT>;
+    static constexpr int q_bytes = GP * HD * 4;
+    static constexpr int p_bytes = kConsumerWarps * kTileRows * GP * 4;
+    static constexpr int o_bytes = kConsumerWarps * GP * HD * 4;
+    static constexpr int ml_bytes = kConsumerWarps * GP * 2 * 4;
+    static constexpr int misc_bytes = 16;
+    static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
+    static __host__ __device__ constexpr int bars_offset(int ns) {
+        return stages_bytes(ns) + q_bytes + p_bytes + o_bytes + ml_bytes + misc_bytes;
+    }
+    static __host__ __device__ constexpr int total(int ns) {
+        return bars_offset(ns) + ns * 2 * 8 + 1024;  // + alignment slack
+    }
+};
+
+// Byte offset inside a TMA-written tile (rows of BOX bytes per box, boxes of
+// 32 rows placed one after another) with the hardware swizzle applied.
+template <int HD, int DT>
+__device__ __forceinline__ uint32_t tile_off(int row, int byte_in_row) {
+    using G = Geo<HD, DT>;
+    const int b = byte_in_row / G::BOX;
+    const uint32_t off =
+        static_cast<uint32_t>(b * kTileRows * G::BOX + row * G::BOX + (byte_in_row % G::BOX));
+    return off ^ (((off >> 7) & G::SWZ) << 4);
+}
+
+// Walks one CTA's slice [b0, b1) of the flattened row space piece by piece.
+struct PieceIter {
+    const PairRow* pairs;
+    int n_pairs, n_kv;
+    long long x, b1;
+    int i;
+    // current piece
+    PairRow pr;
+    int pi, kvh, r, n;
+    long long seg_start;
+
+    __device__ void init(const PairRow* p, int np, int nkv, long long b0_, long long b1_) {
+        pairs = p;
+        n_pairs = np;
+        n_kv = nkv;
+        x = b0_;
+        b1 = b1_;
+        // largest i with pairs[i].off <= x (zero-length pairs share the next offset)
+        int lo = 0, hi = np - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pairs[mid].off <= x) lo = mid; else hi = mid - 1;
+        }
+        i = lo;
+    }
+
+    __device__ bool next() {
+        if (x >= b1) return false;
+        pr = pairs[i];
+        pi = i;
+        const long long rel = x - pr.off;
+        kvh = static_cast<int>(rel / pr.len);
+        r = static_cast<int>(rel - static_cast<long long>(kvh) * pr.len);
+        seg_start = pr.off + static_cast<long long>(kvh) * pr.len;
+        const long long seg_end = seg_start + pr.len;
+        const long long pend = seg_end < b1 ? seg_end : b1;
+        n = static_cast<int>(pend - x);
+        x = pend;
+        if (x == seg_end && kvh == n_kv - 1) {
+            ++i;
+            while (i < n_pairs && pairs[i].len == 0) ++i;
+        }
+        return true;
+    }
+};
+
+// CTA that owns flattened row x when `total` rows are split over P CTAs with
+// CTA c taking [floor(c*total/P), floor((c+1)*total/P)).
+__device__ __forceinline__ long long owner_cta(long long x, long long total, long long P) {
+    return ((x + 1) * P - 1) / total;
+}
+
+// Rotates and stores the k and v slice of kv head `kvh` at row pr.append_row
+// (transformer.cpp:2506-2520), one warp.
+template <int HD, int DT>
+__device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow& pr, int kvh,
+                                             int lane) {
+    const float* kin = a.k_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
+    const float* vin = a.v_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
+    const long long dst = static_cast<long long>(pr.seq) * a.seq_stride +
+                          static_cast<long long>(pr.cache_layer) * a.layer_stride +
+                          static_cast<long long>(pr.append_row) * a.row_stride + kvh * HD;
+    const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
+#pragma unroll 2
+    for (int d = lane; d < HD; d += 32) {
+        const float kr = rope_elem(kin, d, pr.rope_half, cs, a.neox != 0);
+        store_kv<DT>(a.k_cache, dst + d, kr);
+        store_kv<DT>(a.v_cache, dst + d, vin[d]);
+    }
+}
+
+// Writes one merged (g, d) element of a finished segment: normalised output,
+// or the partial (o, m, l) in partial mode.
+template <int HD>
+__device__ __forceinline__ void emit_final(const DecodeArgs& a, const PairRow& pr, int h, int d,
+                                           float M, float L, float O) {
+    if (a.part_out) {
+        const long long base = (static_cast<long long>(pr.io) * a.n_heads + h) * (HD + 2);
+        a.part_out[base + d] = O;
+        if (d == 0) {
+            a.part_out[base + HD] = M;
+            a.part_out[base + HD + 1] = L;
+        }
+    } else {
+        a.out[static_cast<long long>(pr.io) * a.q_stride + h * HD + d] = O * (1.0f / L);
+    }
+}
+
+template <int HD, int GP, int DT>
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                  const DecodeArgs a) {
+    using G = Geo<HD, DT>;
+    using L = SmemLayout<HD, GP, DT>;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+    unsigned char* base = smem_raw + (base_u32 - raw_u32);
+    const int NS = a.n_stages;
+    float* q_s = reinterpret_cast<float*>(base + L::stages_bytes(NS));
+    float* p_s = q_s + GP * HD;
+    float* o_s = p_s + kConsumerWarps * kTileRows * GP;
+    float* ml_s = o_s + kConsumerWarps * GP * HD;
+    int* misc = reinterpret_cast<int*>(ml_s + kConsumerWarps * GP * 2);
+    const uint32_t bars = base_u32 + L::bars_offset(NS);  // full[s] at bars+8s, empty[s] at bars+8(NS+s)
+    volatile int* abort_flag = misc + 1;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(bars + 8 * s, 1);
+            mbar_init(bars + 8 * (NS + s), 1);
+        }
+        misc[0] = 0;
+        misc[1] = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    const long long P = gridDim.x;
+    const long long c = blockIdx.x;
+    const long long b0 = a.total * c / P;
+    const long long b1 = a.total * (c + 1) / P;
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tensormap(&tmK);
+            prefetch_tensormap(&tmV);
+        }
+        PieceIter it;
+        it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1);
+        int tile = 0;
+        int n_issued = 0;  // tiles [0, n_issued) had their loads issued
+        while (it.next()) {
+            const PairRow& pr = it.pr;
+            const int ntiles = (it.n + kTileRows - 1) / kTileRows;
+            int t_app = -1;
+            if (pr.append_row >= 0) {
+                const int al = pr.append_row - pr.row0;
+                if (al >= it.r && al < it.r + it.n) t_app = (al - it.r) / kTileRows;
+            }
+            for (int t = 0; t < ntiles; ++t, ++tile) {
+                if (t == t_app) {
+                    append_slice<HD, DT>(a, pr, it.kvh, lane);
+                    fence_proxy_async_global();
+                    __syncwarp();
+                }
+                const int stage = tile % NS;
+                const int use = tile / NS;
+                if (use > 0)
+                    mbar_wait_bounded(bars + 8 * (NS + stage), (use - 1) & 1, abort_flag, a.err);
+                const bool issue = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+                if (!issue) continue;
+                n_issued = tile + 1;
+                if (lane == 0) {
+                    const uint32_t fb = bars + 8 * stage;
+                    mbar_arrive_expect_tx(fb, 2 * G::TILEB);
+                    const uint32_t dk = base_u32 + stage * 2 * G::TILEB;
+                    const uint32_t dv = dk + G::TILEB;
+                    const int row = pr.row0 + it.r + t * kTileRows;
+#pragma unroll
+                    for (int b = 0; b < G::NB; ++b) {
+                        const int c0 = it.kvh * HD + b * G::BOXE;
+                        tma_load_4d(dk + b * kTileRows * G::BOX, &tmK, fb, c0, row,
+                                    pr.cache_layer, pr.seq);
+                        tma_load_4d(dv + b * kTileRows * G::BOX, &tmV, fb, c0, row,
+                                    pr.cache_layer, pr.seq);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        // Drain: every issued tile load must land before the CTA exits.
+        const int first = n_issued > NS ? n_issued - NS : 0;
+        for (int k = first; k < n_issued; ++k)
+            mbar_wait_bounded(bars + 8 * (k % NS), (k / NS) & 1, abort_flag, a.err, false);
+        return;
+    }
+
+    // ---------------------------------------------------------------- consumers
+    const int ctid = threadIdx.x;
+
+    // Partial mode: pairs with no local rows still owe an (o=0, m=-inf, l=0) partial.
+    if (a.part_out) {
+        for (int i = blockIdx.x; i < a.n_pairs; i += gridDim.x) {
+            const PairRow pr = a.pairs[i];
+            if (pr.len != 0) continue;
+            for (int idx = ctid; idx < a.n_heads * (HD + 2); idx += kConsumerThreads) {
+                const int d = idx % (HD + 2);
+                a.part_out[static_cast<long long>(pr.io) * a.n_heads * (HD + 2) + idx] =
+                    d == HD ? -INFINITY : 0.0f;
+            }
+        }
+    }
+
+    PieceIter it;
+    it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1);
+    int tile = 0;
+    const float scale = a.scale;
+    const float softcap = a.softcap;
+    const float inv_cap = a.inv_softcap;
+    while (it.next()) {
+        const PairRow& pr = it.pr;
+        const int kvh = it.kvh;
+
+        // q rotation for this segment's query group -> q_s (padded heads = 0)
+        named_bar_sync(1, kConsumerThreads);
+        {
+            const float* qin = a.q + static_cast<long long>(pr.io) * a.q_stride +
+                               static_cast<long long>(kvh) * a.G * HD;
+            const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
+            for (int idx = ctid; idx < GP * HD; idx += kConsumerThreads) {
+                const int g = idx / HD, d = idx % HD;
+                q_s[idx] = g < a.G ? rope_elem(qin + g * HD, d, pr.rope_half, cs, a.neox != 0)
+                                   : 0.0f;
+            }
+        }
+        named_bar_sync(1, kConsumerThreads);
+
+        float m[GP], l[GP], o[GP][G::DPL];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) {
+            m[g] = -INFINITY;
+            l[g] = 0.0f;
+#pragma unroll
+            for (int k = 0; k < G::DPL; ++k) o[g][k] = 0.0f;
+        }
+
+        const int ntiles = (it.n + kTileRows - 1) / kTileRows;
+        for (int t = 0; t < ntiles; ++t, ++tile) {
+            if ((tile % kConsumerWarps) != warp) continue;
+            const int stage = tile % NS;
+            mbar_wait_bounded(bars + 8 * stage, (tile / NS) & 1, abort_flag, a.err);
+            const int nvalid = min(kTileRows, it.n - t * kTileRows);
+            const unsigned char* Kt = base + stage * 2 * G::TILEB;
+            const unsigned char* Vt = Kt + G::TILEB;
+
+            // ---- scores: lane = row
+            float s[GP];
+            if (lane < nvalid) {
+                float acc[GP];
+#pragma unroll
+                for (int g = 0; g < GP; ++g) acc[g] = 0.0f;
+#pragma unroll 4
+                for (int j = 0; j < G::CHUNKS; ++j) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(
+                        Kt + tile_off<HD, DT>(lane, j * 16));
+                    float kv[G::EPC];
+                    unpack16<DT>(raw, kv);
+#pragma unroll
+                    for (int e4 = 0; e4 < G::EPC; e4 += 4) {
+#pragma unroll
+                        for (int g = 0; g < GP; ++g) {
+                            const float4 qv =
+                                *reinterpret_cast<const float4*>(q_s + g * HD + j * G::EPC + e4);
+                            acc[g] = __fmaf_rn(qv.x, kv[e4 + 0], acc[g]);
+                            acc[g] = __fmaf_rn(qv.y, kv[e4 + 1], acc[g]);
+                            acc[g] = __fmaf_rn(qv.z, kv[e4 + 2], acc[g]);
+                            acc[g] = __fmaf_rn(qv.w, kv[e4 + 3], acc[g]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int g = 0; g < GP; ++g) {
+                    float sc = __fmul_rn(acc[g], scale);
+                    if (softcap > 0.0f) sc = __fmul_rn(softcap, tanhf(__fmul_rn(sc, inv_cap)));
+                    s[g] = sc;
+                }
+            } else {
+#pragma unroll
+                for (int g = 0; g < GP; ++g) s[g] = -INFINITY;
+            }
+
+            // ---- online softmax over this tile
+            float pv[GP];
+#pragma unroll
+            for (int g = 0; g < GP; ++g) {
+                const float mt = warp_max(s[g]);
+                const float mn = fmaxf(m[g], mt);
+                const float alpha = m[g] == -INFINITY ? 0.0f : ex2_approx((m[g] - mn) * kLog2e);
+                const float p = lane < nvalid ? ex2_approx((s[g] - mn) * kLog2e) : 0.0f;
+                l[g] = l[g] * alpha + p;
+#pragma unroll
+                for (int k = 0; k < G::DPL; ++k) o[g][k] *= alpha;
+                m[g] = mn;
+                pv[g] = p;
+            }
+            float* pw = p_s + warp * kTileRows * GP;
+            if constexpr (GP % 4 == 0) {
+#pragma unroll
+                for (int g4 = 0; g4 < GP; g4 += 4)
+                    *reinterpret_cast<float4*>(pw + lane * GP + g4) =
+                        make_float4(pv[g4], pv[g4 + 1], pv[g4 + 2], pv[g4 + 3]);
+            } else {
+#pragma unroll
+                for (int g = 0; g < GP; ++g) pw[lane * GP + g] = pv[g];
+            }
+            __syncwarp();
+
+            // ---- PV: lane = head dims [lane*DPL, lane*DPL + DPL)
+#pragma unroll 2
+            for (int rr = 0; rr < nvalid; ++rr) {
+                float pr_[GP];
+                if constexpr (GP % 4 == 0) {
+#pragma unroll
+                    for (int g4 = 0; g4 < GP; g4 += 4) {
+                        const float4 t4 = *reinterpret_cast<const float4*>(pw + rr * GP + g4);
+                        pr_[g4] = t4.x;
+                        pr_[g4 + 1] = t4.y;
+                        pr_[g4 + 2] = t4.z;
+                        pr_[g4 + 3] = t4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int g = 0; g < GP; ++g) pr_[g] = pw[rr * GP + g];
+                }
+                float vv[G::DPL];
+                if constexpr (G::LANEB >= 16) {
+#pragma unroll
+                    for (int q16 = 0; q16 < G::LANEB / 16; ++q16) {
+                        const uint4 raw = *reinterpret_cast<const uint4*>(
+                            Vt + tile_off<HD, DT>(rr, lane * G::LANEB + q16 * 16));
+                        unpack16<DT>(raw, vv + q16 * G::EPC);
+                    }
+                } else if constexpr (G::LANEB == 8) {
+                    const uint2 raw =
+                        *reinterpret_cast<const uint2*>(Vt + tile_off<HD, DT>(rr, lane * 8));
+                    if constexpr (DT == DT_F32) {
+                        vv[0] = __uint_as_float(raw.x);
+                        vv[1] = __uint_as_float(raw.y);
+                    } else {
+                        const uint4 r4 = make_uint4(raw.x, raw.y, 0u, 0u);
+                        float tmp[8];
+                        unpack16<DT>(r4, tmp);
+#pragma unroll
+                        for (int k = 0; k < G::DPL; ++k) vv[k] = tmp[k];
+                    }
+                } else if constexpr (G::LANEB == 4) {
+                    const uint32_t raw =
+                        *reinterpret_cast<const uint32_t*>(Vt + tile_off<HD, DT>(rr, lane * 4));
+                    if constexpr (DT == DT_F32) {
+                        vv[0] = __uint_as_float(raw);
+                    } else if constexpr (DT == DT_BF16) {
+                        vv[0] = __uint_as_float(raw << 16);
+                        vv[1] = __uint_as_float(raw & 0xFFFF0000u);
+                    } else {
+                        vv[0] = f16_bits_to_f32(raw & 0xFFFFu);
+                        vv[1] = f16_bits_to_f32(raw >> 16);
+                    }
+                } else {  // 2 bytes: one 16-bit element
+                    const uint32_t raw =
+                        *reinterpret_cast<const uint16_t*>(Vt + tile_off<HD, DT>(rr, lane * 2));
+                    vv[0] = DT == DT_BF16 ? bf16_bits_to_f32(raw) : f16_bits_to_f32(raw);
+                }
+#pragma unroll
+                for (int g = 0; g < GP; ++g)
+#pragma unroll
+                    for (int k = 0; k < G::DPL; ++k) o[g][k] = __fmaf_rn(pr_[g], vv[k], o[g][k]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bars + 8 * (NS + stage));
+        }
+
+        // ---- merge the four warps' states for this piece
+#pragma unroll
+        for (int g = 0; g < GP; ++g) l[g] = warp_sum(l[g]);
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < GP; ++g) {
+                ml_s[(warp * GP + g) * 2] = m[g];
+                ml_s[(warp * GP + g) * 2 + 1] = l[g];
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < GP; ++g)
+#pragma unroll
+            for (int k = 0; k < G::DPL; ++k) o_s[(warp * GP + g) * HD + lane * G::DPL + k] = o[g][k];
+        named_bar_sync(1, kConsumerThreads);
+
+        const bool whole = it.r == 0 && it.n == pr.len;
+        const long long seg = static_cast<long long>(it.pi) * a.n_kv + kvh;
+        const long long slot = c + seg;
+        for (int idx = ctid; idx < a.G * HD; idx += kConsumerThreads) {
+            const int g = idx / HD, d = idx % HD;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml_s[(w * GP + g) * 2]);
+            float Lsum = 0.0f, O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float mw = ml_s[(w * GP + g) * 2];
+                const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
+                Lsum += ml_s[(w * GP + g) * 2 + 1] * f;
+                O += o_s[(w * GP + g) * HD + d] * f;
+            }
+            if (whole) {
+                emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
+            } else {
+                float* dst = a.scratch + (slot * GP + g) * (HD + 2);
+                dst[d] = O;
+                if (d == 0) {
+                    dst[HD] = M;
+                    dst[HD + 1] = Lsum;
+                }
+            }
+        }
+        if (!whole) {
+            // Last CTA to finish this segment merges every piece (no waiting).
+            __threadfence();
+            named_bar_sync(1, kConsumerThreads);
+            const long long c_first = owner_cta(it.seg_start, a.total, P);
+            const long long c_last = owner_cta(it.seg_start + pr.len - 1, a.total, P);
+            if (ctid == 0) {
+                const int prev = atomicAdd(a.counters + seg, 1);
+                const bool last = prev == static_cast<int>(c_last - c_first);
+                misc[0] = last ? 1 : 0;
+                if (last) a.counters[seg] = 0;
+            }
+            named_bar_sync(1, kConsumerThreads);
+            if (misc[0]) {
+                __threadfence();
+                for (int idx = ctid; idx < a.G * HD; idx += kConsumerThreads) {
+                    const int g = idx / HD, d = idx % HD;
+                    float M = -INFINITY;
+                    for (long long cc = c_first; cc <= c_last; ++cc)
+                        M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GP + g) * (HD + 2) + HD));
+                    float Lsum = 0.0f, O = 0.0f;
+                    for (long long cc = c_first; cc <= c_last; ++cc) {
+                        const float* src = a.scratch + ((cc + seg) * GP + g) * (HD + 2);
+                        const float mw = __ldcg(src + HD);
+                        const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
+                        Lsum += __ldcg(src + HD + 1) * f;
+                        O += __ldcg(src + d) * f;
+                    }
+                    emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
+                }
+            }
+        }
+    }
+}
+
+}  // namespace jx

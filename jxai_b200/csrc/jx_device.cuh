@@ -1,0 +1,217 @@
+// jx_device.cuh -- device helpers shared by the decode-attention kernels:
+// inline-PTX wrappers for mbarriers, TMA tile loads and proxy fences, bounded
+// waits, and bit-exact copies of jxai's scalar KV conversions.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace jx {
+
+// ---------------------------------------------------------------- addressing
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------- mbarriers
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes freshly initialised barriers visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// A wait that always ends: after `limit_ns` of wall time it raises the CTA's
+// abort flag and the device error word and returns false.  Once the CTA has
+// aborted, later waits return false at once (the caller carries on through
+// its barriers so that no warp is left waiting on another).
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
+constexpr int kDevErrWaitTimeout = 1;
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* err,
+                                                  bool honour_abort = true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (honour_abort && *abort_flag) return false;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (honour_abort && *abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1;
+            atomicExch(err, kDevErrWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- TMA
+// Tiled 4-D load global -> this CTA's shared memory, completion counted on an
+// mbarrier.  No multicast: every CTA fetches its own tiles.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) reads of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Named barrier over `count` threads (count a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---------------------------------------------------------------- math
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------- KV element conversions
+// Bit-for-bit copies of jxai's scalar conversions (src/quant.cpp:876-939).
+enum { DT_F32 = 0, DT_BF16 = 1, DT_F16T = 2 };
+
+// fp32_to_bf16 (quant.cpp:934-939): round to nearest even, no NaN special case.
+__device__ __forceinline__ uint16_t f32_to_bf16_ref(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return static_cast<uint16_t>((u + (((u >> 16) & 1u) + 0x7FFFu)) >> 16);
+}
+
+// fp32_to_fp16 (quant.cpp:906-925): truncates the mantissa; exponent overflow,
+// Inf and NaN become +-Inf; values below the smallest subnormal become +-0.
+__device__ __forceinline__ uint16_t f32_to_f16_trunc_ref(float f) {
+    const uint32_t u = __float_as_uint(f);
+    const uint32_t sign = (u >> 16) & 0x8000u;
+    const int ex = static_cast<int>((u >> 23) & 0xFFu) - 127 + 15;
+    uint32_t mant = u & 0x007FFFFFu;
+    if (ex <= 0) {
+        if (ex < -10) return static_cast<uint16_t>(sign);
+        mant |= 0x00800000u;
+        return static_cast<uint16_t>(sign | (mant >> (14 - ex)));
+    }
+    if (ex >= 31) return static_cast<uint16_t>(sign | 0x7C00u);
+    return static_cast<uint16_t>(sign | (static_cast<uint32_t>(ex) << 10) | (mant >> 13));
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+// Exact IEEE half -> float (fp16_to_fp32, quant.cpp:876-904).
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+}
+
+template <int DT>
+__device__ __forceinline__ void store_kv(void* base, long long i, float x) {
+    if constexpr (DT == DT_F32) {
+        static_cast<float*>(base)[i] = x;
+    } else if constexpr (DT == DT_BF16) {
+        static_cast<uint16_t*>(base)[i] = f32_to_bf16_ref(x);
+    } else {
+        static_cast<uint16_t*>(base)[i] = f32_to_f16_trunc_ref(x);
+    }
+}
+
+// Unpacks one 16-byte chunk of stored elements into floats.
+template <int DT>
+__device__ __forceinline__ void unpack16(const uint4& r, float* out) {
+    if constexpr (DT == DT_F32) {
+        out[0] = __uint_as_float(r.x);
+        out[1] = __uint_as_float(r.y);
+        out[2] = __uint_as_float(r.z);
+        out[3] = __uint_as_float(r.w);
+    } else {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (DT == DT_BF16) {
+                out[2 * i] = __uint_as_float(w[i] << 16);
+                out[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            } else {
+                out[2 * i] = f16_bits_to_f32(w[i] & 0xFFFFu);
+                out[2 * i + 1] = f16_bits_to_f32(w[i] >> 16);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- RoPE
+// One element of a rotated head, rounded as jxai's build rounds apply_rope
+// (src/transformer.cpp:76-138, gcc -O3 -mfma):
+//   Neox pair (j, j+half):   x[j] = fma(a, c, -(b*s)),  x[j+half] = fma(a, s, b*c)
+//   interleaved (2j, 2j+1):  x[2j] = a*c - b*s,        x[2j+1]   = a*s + b*c
+// Dimensions at or beyond 2*half are returned unchanged.  cs[j] = (cos, sin).
+__device__ __forceinline__ float rope_elem(const float* x, int d, int half, const float2* cs,
+                                           bool neox) {
+    if (d >= 2 * half) return x[d];
+    if (neox) {
+        const int j = d < half ? d : d - half;
+        const float2 t = cs[j];
+        const float a = x[j], b = x[j + half];
+        return d < half ? __fmaf_rn(a, t.x, -__fmul_rn(b, t.y))
+                        : __fmaf_rn(a, t.y, __fmul_rn(b, t.x));
+    }
+    const int j = d >> 1;
+    const float2 t = cs[j];
+    const float a = x[2 * j], b = x[2 * j + 1];
+    return (d & 1) == 0 ? __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y))
+                        : __fadd_rn(__fmul_rn(a, t.y), __fmul_rn(b, t.x));
+}
+
+}  // namespace jx

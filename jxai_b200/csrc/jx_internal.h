@@ -1,0 +1,79 @@
+// jx_internal.h -- types shared by the host library and the kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace jx {
+
+// One (step sequence, call layer) pair of a decode step.  Pairs are stored in
+// step order (sequence-major); `off` is the prefix sum of n_kv*len over the
+// pairs before it, i.e. the pair's first index in the flattened
+// (pair, kv head, attended row) space the persistent CTAs split evenly.
+struct PairRow {
+    long long off;
+    int seq;          // cache sequence
+    int io;           // row of q/k/v/out: step_seq * n_call_layers + call_layer
+    int cache_layer;  // kv_source_layer: cache layer read (and appended)
+    int row0;         // first attended local cache row
+    int len;          // attended local rows (0 only in partial mode)
+    int append_row;   // local row receiving this step's k/v, or -1
+    int rope_row;     // row of the cos/sin table for (rope config, pos)
+    int rope_half;    // rotated pairs per head = min(head_dim, rope_dim) / 2
+    int pad[2];
+};
+static_assert(sizeof(PairRow) == 48, "PairRow layout");
+
+struct DecodeArgs {
+    const PairRow* pairs;
+    int n_pairs;
+    int n_kv;       // kv heads
+    int G;          // query heads per kv head
+    int n_heads;
+    long long total;  // flattened rows
+    const float* q;
+    const float* k_in;
+    const float* v_in;
+    float* out;
+    long long q_stride;   // floats between (seq, layer) rows of q/out
+    long long kv_stride;  // floats between (seq, layer) rows of k/v
+    void* k_cache;
+    void* v_cache;
+    long long seq_stride;    // cache elements between sequences
+    long long layer_stride;  // cache elements between layers
+    long long row_stride;    // cache elements between rows
+    const float2* rope;      // rows of head_dim/2 (cos, sin) pairs
+    float scale;
+    float softcap;
+    float inv_softcap;
+    int neox;
+    float* scratch;  // split partials, (P + n_segments) slots
+    int* counters;   // per segment arrival counters (self-resetting)
+    float* part_out; // partial mode output, or null
+    int* err;        // device error word
+    int n_stages;
+};
+
+// Host-side launch request for one fused decode launch.
+struct DecodeLaunch {
+    DecodeArgs args;
+    const CUtensorMap* tmK;
+    const CUtensorMap* tmV;
+    int head_dim;
+    int gp;      // padded group size (1, 2, 4, 8)
+    int dtype;   // 0 f32, 1 bf16, 2 f16 trunc
+    int grid;
+    int stages;
+    cudaStream_t stream;
+};
+
+// Dynamic shared memory bytes of the kernel for (head_dim, gp, dtype, stages),
+// or -1 when that combination is not compiled.
+int decode_smem_bytes(int head_dim, int gp, int dtype, int stages);
+// Resident CTAs per SM for that configuration (occupancy calculator).
+int decode_ctas_per_sm(int head_dim, int gp, int dtype, int stages);
+// Launches; returns a cudaError_t.
+cudaError_t decode_launch(const DecodeLaunch& L);
+
+}  // namespace jx

@@ -1,0 +1,859 @@
+// jx_lib.cu -- host side of libjxattn.so: the C ABI declared in
+// include/jx_attn.h.  Owns the device KV cache (the B200 counterpart of
+// KVCacheSlot, include/transformer.h:115-131), turns each decode step into a
+// flattened work plan, and launches the fused kernel (jx_decode.cuh), plus the
+// log-sum-exp merge of sequence shards and the seeded fill used by benches.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "jx_attn.h"
+#include "jx_device.cuh"
+#include "jx_internal.h"
+
+namespace jx {
+bool decode_dispatch_dt0(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+bool decode_dispatch_dt1(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+bool decode_dispatch_dt2(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+
+static bool dispatch(int dtype, int hd, int gp, int op, int stages, const DecodeLaunch* L,
+                     int* oi, cudaError_t* oe) {
+    switch (dtype) {
+        case 0: return decode_dispatch_dt0(hd, gp, op, stages, L, oi, oe);
+        case 1: return decode_dispatch_dt1(hd, gp, op, stages, L, oi, oe);
+        case 2: return decode_dispatch_dt2(hd, gp, op, stages, L, oi, oe);
+        default: return false;
+    }
+}
+
+int decode_smem_bytes(int hd, int gp, int dtype, int stages) {
+    int v = -1;
+    cudaError_t e = cudaSuccess;
+    if (!dispatch(dtype, hd, gp, 0, stages, nullptr, &v, &e)) return -1;
+    return v;
+}
+
+int decode_ctas_per_sm(int hd, int gp, int dtype, int stages) {
+    int v = 0;
+    cudaError_t e = cudaSuccess;
+    if (!dispatch(dtype, hd, gp, 1, stages, nullptr, &v, &e)) return 0;
+    return v;
+}
+
+cudaError_t decode_launch(const DecodeLaunch& L) {
+    int v = 0;
+    cudaError_t e = cudaErrorInvalidValue;
+    if (!dispatch(L.dtype, L.head_dim, L.gp, 2, L.stages, &L, &v, &e)) return cudaErrorInvalidValue;
+    return e;
+}
+
+// ------------------------------------------------------------------ kernels
+
+__global__ void lse_merge_kernel(const float* __restrict__ gathered, int n_shards,
+                                 long long shard_stride, int n_rows, int n_heads, int hd,
+                                 float* __restrict__ out, long long out_stride) {
+    const int row = blockIdx.x;  // (group, head)
+    if (row >= n_rows) return;
+    const int grp = row / n_heads, h = row % n_heads;
+    const long long base = static_cast<long long>(row) * (hd + 2);
+    float M = -INFINITY;
+    for (int r = 0; r < n_shards; ++r) M = fmaxf(M, gathered[r * shard_stride + base + hd]);
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+        float Ls = 0.0f, O = 0.0f;
+        for (int r = 0; r < n_shards; ++r) {
+            const float* src = gathered + r * shard_stride + base;
+            const float m = src[hd];
+            const float f = m == -INFINITY ? 0.0f : ex2_approx((m - M) * 1.4426950408889634f);
+            Ls += src[hd + 1] * f;
+            O += src[d] * f;
+        }
+        out[static_cast<long long>(grp) * out_stride + static_cast<long long>(h) * hd + d] =
+            O * (1.0f / Ls);
+    }
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+// Counter-based N(0,1): splitmix64 of (seed, stream, index) -> Box-Muller.
+__device__ __forceinline__ float normal_at(uint64_t seed, uint32_t stream_id, uint64_t idx) {
+    const uint64_t h = splitmix64(seed ^ splitmix64((static_cast<uint64_t>(stream_id) << 56) ^ idx));
+    const float u1 = (static_cast<float>(h >> 40) + 1.0f) * (1.0f / 16777216.0f);
+    const float u2 = static_cast<float>(h & 0xFFFFFFull) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+template <int DT>
+__global__ void fill_cache_kernel(void* k, void* v, const uint32_t* __restrict__ rows,
+                                  uint32_t n_seqs, uint32_t n_layers, uint32_t cap, uint32_t rs,
+                                  uint64_t seed) {
+    const long long per_seq = static_cast<long long>(n_layers) * cap * rs;
+    const long long total = per_seq * n_seqs;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const uint32_t s = static_cast<uint32_t>(i / per_seq);
+        const uint32_t row = static_cast<uint32_t>((i / rs) % cap);
+        if (row >= rows[s]) continue;
+        store_kv<DT>(k, i, normal_at(seed, 1, static_cast<uint64_t>(i)));
+        store_kv<DT>(v, i, normal_at(seed, 2, static_cast<uint64_t>(i)));
+    }
+}
+
+__global__ void fill_f32_kernel(float* dst, uint64_t n, uint64_t seed, uint32_t stream_id) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = normal_at(seed, stream_id, i);
+}
+
+}  // namespace jx
+
+using namespace jx;
+
+// ------------------------------------------------------------------ errors
+
+static thread_local std::string g_err;
+
+static int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define JX_CUDA(call)                                                                    \
+    do {                                                                                 \
+        cudaError_t e_ = (call);                                                         \
+        if (e_ != cudaSuccess)                                                           \
+            return fail(JX_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));    \
+    } while (0)
+
+namespace {
+
+// Sets the handle's device for the duration of a call and restores the
+// caller's current device afterwards.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) return;
+        ok = prev == dev || cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        if (ok && prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                             cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+struct PlanSlot {
+    std::vector<unsigned char> cached;  // bytes last uploaded
+    void* d_buf = nullptr;
+    size_t d_cap = 0;
+    void* h_buf = nullptr;  // pinned staging
+    size_t h_cap = 0;
+    cudaEvent_t ev = nullptr;
+    bool ev_pending = false;
+};
+
+}  // namespace
+
+struct jx_kv {
+    jx_kv_desc d{};
+    size_t esz = 4;
+    void* k = nullptr;
+    void* v = nullptr;
+    long long seq_stride = 0, layer_stride = 0;  // elements
+    // tensor maps by TMA box inner extent: [0] = 128-byte boxes, [1] = 64-byte boxes
+    CUtensorMap tmK[2], tmV[2];
+    bool tm_ok[2] = {false, false};
+    std::vector<uint32_t> seq_pos;
+    int num_sms = 0;
+    int* d_err = nullptr;
+    uint32_t* d_rows = nullptr;  // fill helper
+    float* d_scratch = nullptr;
+    size_t scratch_floats = 0;
+    int* d_counters = nullptr;
+    size_t counters_n = 0;
+    std::vector<PlanSlot> slots;
+    int opt_ctas_per_sm = 0, opt_stages = 0, opt_grid = 0;
+    int last_launches = 0;
+    // launch shape per (head_dim, group, stages override): {stages, ctas per SM}
+    std::map<std::tuple<int, int, int, int>, std::pair<int, int>> shapes;
+};
+
+namespace {
+
+int encode_maps(jx_kv* kv, int box_kind) {
+    if (kv->tm_ok[box_kind]) return JX_OK;
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(JX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[4] = {kv->d.row_stride, kv->d.capacity, kv->d.n_layers, kv->d.n_seqs};
+    const cuuint64_t strides[3] = {
+        static_cast<cuuint64_t>(kv->d.row_stride) * kv->esz,
+        static_cast<cuuint64_t>(kv->d.row_stride) * kv->esz * kv->d.capacity,
+        static_cast<cuuint64_t>(kv->d.row_stride) * kv->esz * kv->d.capacity * kv->d.n_layers};
+    const uint32_t box_bytes = box_kind == 0 ? 128 : 64;
+    const cuuint32_t box[4] = {static_cast<cuuint32_t>(box_bytes / kv->esz), 32, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUtensorMapDataType dt =
+        kv->esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const CUtensorMapSwizzle sw =
+        box_kind == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    for (int which = 0; which < 2; ++which) {
+        CUresult r = enc(which == 0 ? &kv->tmK[box_kind] : &kv->tmV[box_kind], dt, 4,
+                         which == 0 ? kv->k : kv->v, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(JX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    }
+    kv->tm_ok[box_kind] = true;
+    return JX_OK;
+}
+
+// Default pipeline depth / residency for one kernel configuration: the
+// deepest ring (<= 8 stages) that still lets two CTAs share an SM, else one
+// CTA with the deepest ring that fits.
+void default_shape(int hd, int gp, int dtype, int* stages, int* cps) {
+    const int per_sm = 227 * 1024;
+    int best = 0;
+    for (int ns = 8; ns >= 2; --ns)
+        if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 <= per_sm / 2) { best = ns; break; }
+    if (best) {
+        *stages = best;
+        *cps = 2;
+        return;
+    }
+    for (int ns = 8; ns >= 2; --ns)
+        if (decode_smem_bytes(hd, gp, dtype, ns) <= per_sm) { best = ns; break; }
+    *stages = best ? best : 2;
+    *cps = 1;
+}
+
+int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& bytes,
+                cudaStream_t stream) {
+    if (kv->slots.size() <= slot_i) kv->slots.resize(slot_i + 1);
+    PlanSlot& s = kv->slots[slot_i];
+    if (s.cached == bytes && s.d_buf) return JX_OK;
+    if (s.d_cap < bytes.size()) {
+        if (s.d_buf) JX_CUDA(cudaFree(s.d_buf));
+        s.d_buf = nullptr;
+        s.d_cap = 0;
+        const size_t cap = std::max<size_t>(bytes.size() * 2, 4096);
+        if (cudaMalloc(&s.d_buf, cap) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "plan buffer allocation of %zu bytes failed", cap);
+        s.d_cap = cap;
+    }
+    if (!s.ev) JX_CUDA(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
+    if (s.ev_pending) {
+        JX_CUDA(cudaEventSynchronize(s.ev));
+        s.ev_pending = false;
+    }
+    if (s.h_cap < bytes.size()) {
+        if (s.h_buf) JX_CUDA(cudaFreeHost(s.h_buf));
+        s.h_buf = nullptr;
+        s.h_cap = 0;
+        const size_t cap = std::max<size_t>(bytes.size() * 2, 4096);
+        if (cudaHostAlloc(&s.h_buf, cap, cudaHostAllocDefault) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "pinned staging allocation of %zu bytes failed", cap);
+        s.h_cap = cap;
+    }
+    std::memcpy(s.h_buf, bytes.data(), bytes.size());
+    JX_CUDA(cudaMemcpyAsync(s.d_buf, s.h_buf, bytes.size(), cudaMemcpyHostToDevice, stream));
+    JX_CUDA(cudaEventRecord(s.ev, stream));
+    s.ev_pending = true;
+    s.cached = bytes;
+    return JX_OK;
+}
+
+int ensure_scratch(jx_kv* kv, size_t floats, size_t counters) {
+    if (kv->scratch_floats < floats) {
+        if (kv->d_scratch) JX_CUDA(cudaFree(kv->d_scratch));
+        kv->d_scratch = nullptr;
+        kv->scratch_floats = 0;
+        if (cudaMalloc(&kv->d_scratch, floats * sizeof(float)) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "scratch allocation of %zu floats failed", floats);
+        kv->scratch_floats = floats;
+    }
+    if (kv->counters_n < counters) {
+        if (kv->d_counters) JX_CUDA(cudaFree(kv->d_counters));
+        kv->d_counters = nullptr;
+        kv->counters_n = 0;
+        if (cudaMalloc(&kv->d_counters, counters * sizeof(int)) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "counter allocation failed");
+        JX_CUDA(cudaMemset(kv->d_counters, 0, counters * sizeof(int)));
+        kv->counters_n = counters;
+    }
+    return JX_OK;
+}
+
+// (cos, sin) of every rotated pair at `pos`, computed with the same float
+// expressions as apply_rope (src/transformer.cpp:82-92, 112-116).
+void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
+              bool neox, const float* rope_freqs, float2* out, int width) {
+    const uint32_t rdim = std::min(head_dim, rope_dim);
+    const float pos_scaled = static_cast<float>(pos) / std::max(1e-4f, yarn_scale);
+    const uint32_t half = rdim / 2;
+    for (int j = 0; j < width; ++j) out[j] = make_float2(0.0f, 0.0f);
+    for (uint32_t j = 0; j < half; ++j) {
+        float freq;
+        if (neox) {
+            freq = 1.0f / std::pow(base, (2.0f * static_cast<float>(j)) / static_cast<float>(rdim));
+            if (rope_freqs) freq /= rope_freqs[j];
+        } else {
+            const uint32_t d = 2 * j;
+            freq = 1.0f / std::pow(base, static_cast<float>(d) / static_cast<float>(rdim));
+        }
+        const float angle = pos_scaled * freq;
+        out[j] = make_float2(std::cos(angle), std::sin(angle));
+    }
+}
+
+uint64_t hash_floats(const float* p, size_t n) {
+    uint64_t h = 1469598103934665603ull;
+    const unsigned char* b = reinterpret_cast<const unsigned char*>(p);
+    for (size_t i = 0; i < n * 4; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return h;
+}
+
+int gp_of(uint32_t g) {
+    if (g <= 1) return 1;
+    if (g <= 2) return 2;
+    if (g <= 4) return 4;
+    if (g <= 8) return 8;
+    return 0;
+}
+
+int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
+              float* partials, cudaStream_t stream) {
+    if (!kv || !layers || !a) return fail(JX_ERR_INVALID, "null handle, layers or args");
+    if (n_layers == 0 || a->n_seqs == 0) return fail(JX_ERR_INVALID, "empty step");
+    if (!a->pos || !a->q || !a->k || !a->v) return fail(JX_ERR_INVALID, "null pos/q/k/v");
+    const bool partial = partials != nullptr;
+    if (!partial && !a->out) return fail(JX_ERR_INVALID, "null out");
+    if (a->n_kv_heads == 0 || a->n_heads == 0 || a->n_heads % a->n_kv_heads != 0)
+        return fail(JX_ERR_UNSUPPORTED, "n_heads (%u) must be a multiple of n_kv_heads (%u)",
+                    a->n_heads, a->n_kv_heads);
+    const uint32_t G = a->n_heads / a->n_kv_heads;
+    const int gp = gp_of(G);
+    if (!gp) return fail(JX_ERR_UNSUPPORTED, "query group of %u heads exceeds 8", G);
+    if (!(a->yarn_scale > 0.0f) && a->yarn_scale != 0.0f)
+        return fail(JX_ERR_INVALID, "yarn_scale must not be negative or NaN");
+    const jx_kv_desc& D = kv->d;
+    std::vector<int> seqs(a->n_seqs);
+    {
+        std::vector<char> seen(D.n_seqs, 0);
+        for (uint32_t s = 0; s < a->n_seqs; ++s) {
+            const int sid = a->seq_ids ? a->seq_ids[s] : static_cast<int>(s);
+            if (sid < 0 || static_cast<uint32_t>(sid) >= D.n_seqs)
+                return fail(JX_ERR_INVALID, "sequence id %d outside [0, %u)", sid, D.n_seqs);
+            if (seen[sid]) return fail(JX_ERR_INVALID, "sequence id %d listed twice", sid);
+            seen[sid] = 1;
+            seqs[s] = sid;
+            if (a->pos[s] < 0) return fail(JX_ERR_INVALID, "negative position");
+        }
+    }
+    std::vector<char> appended(D.n_layers, 0);
+    for (uint32_t l = 0; l < n_layers; ++l) {
+        const jx_layer_desc& L = layers[l];
+        const uint32_t hd = L.head_dim;
+        if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
+            return fail(JX_ERR_UNSUPPORTED, "head_dim %u (compiled: 32, 64, 128, 256)", hd);
+        if (hd * kv->esz < 64)
+            return fail(JX_ERR_UNSUPPORTED, "head rows below 64 bytes are not supported");
+        if (static_cast<uint64_t>(a->n_kv_heads) * hd > D.row_stride)
+            return fail(JX_ERR_INVALID, "layer %u: kv_dim %u exceeds row_stride %u", l,
+                        a->n_kv_heads * hd, D.row_stride);
+        if (L.kv_source_layer >= D.n_layers)
+            return fail(JX_ERR_INVALID, "layer %u: kv_source_layer %u >= %u", l, L.kv_source_layer,
+                        D.n_layers);
+        if (a->q_stride < a->n_heads * hd || a->kv_stride < a->n_kv_heads * hd)
+            return fail(JX_ERR_INVALID, "q_stride/kv_stride smaller than the layer's rows");
+        if (!L.shares_kv) appended[L.kv_source_layer] = 1;
+    }
+    const bool neox = a->rope_neox != 0;
+    const float inv_cap = a->softcap > 0.0f ? 1.0f / a->softcap : 0.0f;
+
+    // Launch groups: wave 0 = layers that do not read a cache layer appended
+    // in this call by another layer; wave 1 = the rest.  Within a wave, one
+    // launch per head_dim.
+    struct Group {
+        int hd;
+        std::vector<uint32_t> layers;
+    };
+    std::vector<Group> groups;
+    for (int wave = 0; wave < 2; ++wave) {
+        const size_t first = groups.size();
+        for (uint32_t l = 0; l < n_layers; ++l) {
+            const jx_layer_desc& L = layers[l];
+            const int w = (L.shares_kv && appended[L.kv_source_layer]) ? 1 : 0;
+            if (w != wave) continue;
+            Group* g = nullptr;
+            for (size_t i = first; i < groups.size(); ++i)
+                if (groups[i].hd == static_cast<int>(L.head_dim)) g = &groups[i];
+            if (!g) {
+                groups.push_back(Group{static_cast<int>(L.head_dim), {}});
+                g = &groups.back();
+            }
+            g->layers.push_back(l);
+        }
+    }
+
+    DeviceGuard guard(D.device);
+    if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", D.device);
+    int launches = 0;
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+        const Group& grp = groups[gi];
+        const int hd = grp.hd;
+        const int box_kind = hd * kv->esz >= 128 ? 0 : 1;
+        int rc = encode_maps(kv, box_kind);
+        if (rc) return rc;
+        // ---- pairs and rope rows
+        std::vector<PairRow> pairs;
+        pairs.reserve(static_cast<size_t>(a->n_seqs) * grp.layers.size());
+        std::map<std::tuple<uint32_t, uint32_t, uint32_t, uint32_t, uint64_t, uint32_t>, int>
+            rope_ids;
+        std::vector<float2> rope;
+        const int width = hd / 2;
+        long long off = 0;
+        for (uint32_t s = 0; s < a->n_seqs; ++s) {
+            const uint32_t pos = static_cast<uint32_t>(a->pos[s]);
+            for (uint32_t l : grp.layers) {
+                const jx_layer_desc& L = layers[l];
+                const uint32_t W = a->sliding_window;
+                const uint64_t t0 = (L.is_swa && W > 0 && pos >= W) ? pos - W + 1 : 0;
+                const uint64_t lo = std::max<uint64_t>(t0, D.pos_base);
+                const uint64_t hi =
+                    std::min<uint64_t>(pos, static_cast<uint64_t>(D.pos_base) + D.capacity - 1);
+                const long long len = hi >= lo ? static_cast<long long>(hi - lo + 1) : 0;
+                if (!partial && (lo != t0 || hi != pos))
+                    return fail(JX_ERR_RANGE,
+                                "position %u (window start %llu) is outside the cache rows "
+                                "[%u, %llu); compact or roll back first",
+                                pos, static_cast<unsigned long long>(t0), D.pos_base,
+                                static_cast<unsigned long long>(D.pos_base) + D.capacity);
+                PairRow pr{};
+                pr.off = off;
+                pr.seq = seqs[s];
+                pr.io = static_cast<int>(s * n_layers + l);
+                pr.cache_layer = static_cast<int>(L.kv_source_layer);
+                pr.row0 = len > 0 ? static_cast<int>(lo - D.pos_base) : 0;
+                pr.len = static_cast<int>(len);
+                pr.append_row = (!L.shares_kv && pos >= D.pos_base &&
+                                 static_cast<uint64_t>(pos) <
+                                     static_cast<uint64_t>(D.pos_base) + D.capacity)
+                                    ? static_cast<int>(pos - D.pos_base)
+                                    : -1;
+                const uint32_t rdim = std::min(L.head_dim, L.rope_dim);
+                pr.rope_half = static_cast<int>(rdim / 2);
+                const float* rf = (neox && !L.is_swa && L.rope_freqs) ? L.rope_freqs : nullptr;
+                uint32_t base_bits, yarn_bits;
+                std::memcpy(&base_bits, &L.rope_freq_base, 4);
+                std::memcpy(&yarn_bits, &a->yarn_scale, 4);
+                const uint64_t fh = rf ? hash_floats(rf, rdim / 2) : 0;
+                const auto key = std::make_tuple(rdim, base_bits, yarn_bits, pos, fh,
+                                                 static_cast<uint32_t>(L.head_dim));
+                auto itk = rope_ids.find(key);
+                int rid;
+                if (itk == rope_ids.end()) {
+                    rid = static_cast<int>(rope_ids.size());
+                    rope_ids.emplace(key, rid);
+                    rope.resize(rope.size() + width);
+                    rope_row(L.head_dim, L.rope_dim, pos, L.rope_freq_base, a->yarn_scale, neox,
+                             rf, rope.data() + static_cast<size_t>(rid) * width, width);
+                } else {
+                    rid = itk->second;
+                }
+                pr.rope_row = rid;
+                pairs.push_back(pr);
+                off += len * a->n_kv_heads;
+            }
+        }
+        const long long total = off;
+        const size_t pair_bytes = pairs.size() * sizeof(PairRow);
+        const size_t rope_off = (pair_bytes + 255) & ~static_cast<size_t>(255);
+        std::vector<unsigned char> bytes(rope_off + rope.size() * sizeof(float2), 0);
+        std::memcpy(bytes.data(), pairs.data(), pair_bytes);
+        if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope.size() * sizeof(float2));
+        rc = upload_plan(kv, gi, bytes, stream);
+        if (rc) return rc;
+
+        // ---- launch shape (cached per configuration)
+        int stages = 0, cps = 0;
+        const auto skey = std::make_tuple(hd, gp, kv->opt_stages, kv->opt_ctas_per_sm);
+        auto sit = kv->shapes.find(skey);
+        if (sit != kv->shapes.end()) {
+            stages = sit->second.first;
+            cps = sit->second.second;
+        } else {
+            default_shape(hd, gp, D.dtype, &stages, &cps);
+            if (kv->opt_stages) stages = kv->opt_stages;
+            if (decode_smem_bytes(hd, gp, D.dtype, stages) < 0)
+                return fail(JX_ERR_UNSUPPORTED, "no kernel for head_dim %d group %d dtype %d", hd,
+                            gp, D.dtype);
+            const int occ = decode_ctas_per_sm(hd, gp, D.dtype, stages);
+            if (occ <= 0)
+                return fail(JX_ERR_UNSUPPORTED, "kernel does not fit with %d stages", stages);
+            if (kv->opt_ctas_per_sm) cps = kv->opt_ctas_per_sm;
+            cps = std::max(1, std::min(cps, occ));
+            kv->shapes.emplace(skey, std::make_pair(stages, cps));
+        }
+        long long P = static_cast<long long>(kv->num_sms) * cps;
+        P = std::min<long long>(P, std::max<long long>(1, (total + 63) / 64));
+        if (kv->opt_grid) P = kv->opt_grid;
+        if (total == 0) P = 1;
+        const long long n_segs = static_cast<long long>(pairs.size()) * a->n_kv_heads;
+        rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * (hd + 2),
+                            static_cast<size_t>(std::max<long long>(n_segs, 1)));
+        if (rc) return rc;
+
+        DecodeLaunch Lc{};
+        DecodeArgs& A = Lc.args;
+        A.pairs = static_cast<const PairRow*>(kv->slots[gi].d_buf);
+        A.n_pairs = static_cast<int>(pairs.size());
+        A.n_kv = static_cast<int>(a->n_kv_heads);
+        A.G = static_cast<int>(G);
+        A.n_heads = static_cast<int>(a->n_heads);
+        A.total = total;
+        A.q = a->q;
+        A.k_in = a->k;
+        A.v_in = a->v;
+        A.out = a->out;
+        A.q_stride = a->q_stride;
+        A.kv_stride = a->kv_stride;
+        A.k_cache = kv->k;
+        A.v_cache = kv->v;
+        A.seq_stride = kv->seq_stride;
+        A.layer_stride = kv->layer_stride;
+        A.row_stride = D.row_stride;
+        A.rope = reinterpret_cast<const float2*>(static_cast<unsigned char*>(kv->slots[gi].d_buf) +
+                                                 rope_off);
+        A.scale = a->scale;
+        A.softcap = a->softcap;
+        A.inv_softcap = inv_cap;
+        A.neox = neox ? 1 : 0;
+        A.scratch = kv->d_scratch;
+        A.counters = kv->d_counters;
+        A.part_out = partial ? partials : nullptr;
+        A.err = kv->d_err;
+        A.n_stages = stages;
+        Lc.tmK = &kv->tmK[box_kind];
+        Lc.tmV = &kv->tmV[box_kind];
+        Lc.head_dim = hd;
+        Lc.gp = gp;
+        Lc.dtype = D.dtype;
+        Lc.grid = static_cast<int>(P);
+        Lc.stages = stages;
+        Lc.stream = stream;
+        if (total == 0 && !partial) continue;
+        const cudaError_t e = decode_launch(Lc);
+        if (e != cudaSuccess)
+            return fail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+        ++launches;
+    }
+    kv->last_launches = launches;
+    return JX_OK;
+}
+
+}  // namespace
+
+// ================================================================== C ABI
+
+extern "C" {
+
+const char* jx_last_error_string(void) { return g_err.c_str(); }
+
+const char* jx_version(void) { return "jxai_b200 decode-attention 0.1 (sm_100a)"; }
+
+int jx_kv_create(const jx_kv_desc* desc, jx_kv** out) {
+    if (!desc || !out) return fail(JX_ERR_INVALID, "null desc/out");
+    *out = nullptr;
+    const jx_kv_desc& d = *desc;
+    if (d.n_seqs == 0 || d.n_layers == 0 || d.capacity == 0 || d.row_stride == 0)
+        return fail(JX_ERR_INVALID, "n_seqs, n_layers, capacity and row_stride must be positive");
+    if (d.dtype < 0 || d.dtype > 2) return fail(JX_ERR_INVALID, "unknown dtype %d", d.dtype);
+    const size_t esz = d.dtype == JX_F32 ? 4 : 2;
+    if ((d.row_stride * esz) % 16 != 0)
+        return fail(JX_ERR_UNSUPPORTED, "row_stride*element size must be a multiple of 16 bytes");
+    if (static_cast<uint64_t>(d.pos_base) + d.capacity > (1ull << 31))
+        return fail(JX_ERR_INVALID, "positions must stay below 2^31");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+        return fail(JX_ERR_CUDA, "no CUDA device (this library has no CPU path)");
+    if (d.device < 0 || d.device >= ndev) return fail(JX_ERR_INVALID, "device %d absent", d.device);
+    DeviceGuard guard(d.device);
+    if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", d.device);
+    cudaDeviceProp prop;
+    JX_CUDA(cudaGetDeviceProperties(&prop, d.device));
+    if (prop.major < 10)
+        return fail(JX_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", d.device,
+                    prop.major, prop.minor);
+    jx_kv* kv = new jx_kv();
+    kv->d = d;
+    kv->esz = esz;
+    kv->num_sms = prop.multiProcessorCount;
+    kv->layer_stride = static_cast<long long>(d.capacity) * d.row_stride;
+    kv->seq_stride = kv->layer_stride * d.n_layers;
+    kv->seq_pos.assign(d.n_seqs, 0);
+    const size_t bytes = static_cast<size_t>(kv->seq_stride) * d.n_seqs * esz;
+    auto cleanup = [&](int code) {
+        jx_kv_destroy(kv);
+        return code;
+    };
+    if (cudaMalloc(&kv->k, bytes) != cudaSuccess || cudaMalloc(&kv->v, bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return cleanup(fail(JX_ERR_NOMEM, "KV cache allocation of 2 x %zu bytes failed", bytes));
+    }
+    if (cudaMemset(kv->k, 0, bytes) != cudaSuccess || cudaMemset(kv->v, 0, bytes) != cudaSuccess ||
+        cudaMalloc(&kv->d_err, sizeof(int)) != cudaSuccess ||
+        cudaMemset(kv->d_err, 0, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&kv->d_rows, sizeof(uint32_t) * d.n_seqs) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+        return cleanup(fail(JX_ERR_CUDA, "cache initialisation failed"));
+    *out = kv;
+    return JX_OK;
+}
+
+int jx_kv_destroy(jx_kv* kv) {
+    if (!kv) return JX_OK;
+    DeviceGuard guard(kv->d.device);
+    cudaDeviceSynchronize();
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    cudaFree(kv->d_err);
+    cudaFree(kv->d_rows);
+    cudaFree(kv->d_scratch);
+    cudaFree(kv->d_counters);
+    for (PlanSlot& s : kv->slots) {
+        if (s.ev) cudaEventDestroy(s.ev);
+        cudaFree(s.d_buf);
+        if (s.h_buf) cudaFreeHost(s.h_buf);
+    }
+    delete kv;
+    return JX_OK;
+}
+
+int jx_kv_get_desc(const jx_kv* kv, jx_kv_desc* desc) {
+    if (!kv || !desc) return fail(JX_ERR_INVALID, "null argument");
+    *desc = kv->d;
+    return JX_OK;
+}
+
+int jx_kv_get_seq_pos(const jx_kv* kv, uint32_t seq, uint32_t* seq_pos) {
+    if (!kv || !seq_pos || seq >= kv->d.n_seqs) return fail(JX_ERR_INVALID, "bad handle/sequence");
+    *seq_pos = kv->seq_pos[seq];
+    return JX_OK;
+}
+
+int jx_kv_set_seq_pos(jx_kv* kv, uint32_t seq, uint32_t seq_pos) {
+    if (!kv || seq >= kv->d.n_seqs) return fail(JX_ERR_INVALID, "bad handle/sequence");
+    if (seq_pos > kv->d.capacity) return fail(JX_ERR_RANGE, "seq_pos beyond capacity");
+    kv->seq_pos[seq] = seq_pos;
+    return JX_OK;
+}
+
+int jx_kv_clear(jx_kv* kv, uint32_t seq, void* stream) {
+    if (!kv || seq >= kv->d.n_seqs) return fail(JX_ERR_INVALID, "bad handle/sequence");
+    DeviceGuard guard(kv->d.device);
+    const size_t bytes = static_cast<size_t>(kv->seq_stride) * kv->esz;
+    const size_t off = static_cast<size_t>(seq) * bytes;
+    JX_CUDA(cudaMemsetAsync(static_cast<char*>(kv->k) + off, 0, bytes, (cudaStream_t)stream));
+    JX_CUDA(cudaMemsetAsync(static_cast<char*>(kv->v) + off, 0, bytes, (cudaStream_t)stream));
+    kv->seq_pos[seq] = 0;
+    return JX_OK;
+}
+
+int jx_kv_rollback(jx_kv* kv, uint32_t seq, uint32_t new_seq_pos) {
+    if (!kv || seq >= kv->d.n_seqs) return fail(JX_ERR_INVALID, "bad handle/sequence");
+    if (new_seq_pos < kv->seq_pos[seq]) kv->seq_pos[seq] = new_seq_pos;
+    return JX_OK;
+}
+
+int jx_kv_compact(jx_kv* kv, uint32_t seq, uint32_t keep_recent, void* stream) {
+    if (!kv || seq >= kv->d.n_seqs) return fail(JX_ERR_INVALID, "bad handle/sequence");
+    const uint32_t sink = 4;
+    const uint32_t sp = kv->seq_pos[seq];
+    if (sp <= sink + keep_recent) return JX_OK;
+    DeviceGuard guard(kv->d.device);
+    const uint32_t src_start = sp - keep_recent;
+    const size_t row_b = static_cast<size_t>(kv->d.row_stride) * kv->esz;
+    const size_t layer_b = static_cast<size_t>(kv->layer_stride) * kv->esz;
+    const size_t width = static_cast<size_t>(keep_recent) * row_b;
+    const size_t seq_off = static_cast<size_t>(seq) * kv->seq_stride * kv->esz;
+    cudaStream_t st = (cudaStream_t)stream;
+    void* tmp = nullptr;
+    // Source and destination overlap (the reference uses memmove), so the
+    // kept rows go through a temporary buffer: one 2-D copy out, one back.
+    if (width > 0) {
+        if (cudaMalloc(&tmp, width * kv->d.n_layers) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "compaction buffer allocation failed");
+        for (int which = 0; which < 2; ++which) {
+            char* basep = static_cast<char*>(which == 0 ? kv->k : kv->v) + seq_off;
+            cudaError_t e = cudaMemcpy2DAsync(tmp, width, basep + src_start * row_b, layer_b, width,
+                                              kv->d.n_layers, cudaMemcpyDeviceToDevice, st);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(basep + sink * row_b, layer_b, tmp, width, width,
+                                      kv->d.n_layers, cudaMemcpyDeviceToDevice, st);
+            if (e != cudaSuccess) {
+                cudaFree(tmp);
+                return fail(JX_ERR_CUDA, "compaction copy failed: %s", cudaGetErrorString(e));
+            }
+        }
+        JX_CUDA(cudaStreamSynchronize(st));
+        JX_CUDA(cudaFree(tmp));
+    }
+    kv->seq_pos[seq] = sink + keep_recent;
+    return JX_OK;
+}
+
+int jx_kv_copy_rows(jx_kv* kv, uint32_t seq, uint32_t layer, int which, uint32_t row0,
+                    uint32_t n_rows, void* buf, int to_cache, void* stream) {
+    if (!kv || !buf || seq >= kv->d.n_seqs || layer >= kv->d.n_layers || (which != 0 && which != 1))
+        return fail(JX_ERR_INVALID, "bad copy_rows arguments");
+    if (static_cast<uint64_t>(row0) + n_rows > kv->d.capacity)
+        return fail(JX_ERR_RANGE, "rows [%u, %u) beyond capacity %u", row0, row0 + n_rows,
+                    kv->d.capacity);
+    DeviceGuard guard(kv->d.device);
+    const size_t row_b = static_cast<size_t>(kv->d.row_stride) * kv->esz;
+    char* p = static_cast<char*>(which == 0 ? kv->k : kv->v) +
+              (static_cast<size_t>(seq) * kv->seq_stride +
+               static_cast<size_t>(layer) * kv->layer_stride) * kv->esz +
+              static_cast<size_t>(row0) * row_b;
+    const size_t n = static_cast<size_t>(n_rows) * row_b;
+    if (to_cache)
+        JX_CUDA(cudaMemcpyAsync(p, buf, n, cudaMemcpyDefault, (cudaStream_t)stream));
+    else
+        JX_CUDA(cudaMemcpyAsync(buf, p, n, cudaMemcpyDefault, (cudaStream_t)stream));
+    return JX_OK;
+}
+
+int jx_kv_layer_ptr(jx_kv* kv, uint32_t seq, uint32_t layer, int which, void** ptr) {
+    if (!kv || !ptr || seq >= kv->d.n_seqs || layer >= kv->d.n_layers || (which != 0 && which != 1))
+        return fail(JX_ERR_INVALID, "bad layer_ptr arguments");
+    *ptr = static_cast<char*>(which == 0 ? kv->k : kv->v) +
+           (static_cast<size_t>(seq) * kv->seq_stride + static_cast<size_t>(layer) * kv->layer_stride) *
+               kv->esz;
+    return JX_OK;
+}
+
+int jx_attn_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                 const jx_step_args* args, void* stream) {
+    return step_impl(kv, layers, n_layers, args, nullptr, (cudaStream_t)stream);
+}
+
+int jx_attn_step_partial(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                         const jx_step_args* args, float* partials, void* stream) {
+    if (!partials) return fail(JX_ERR_INVALID, "null partials");
+    return step_impl(kv, layers, n_layers, args, partials, (cudaStream_t)stream);
+}
+
+int jx_lse_merge(const float* gathered, uint32_t n_shards, uint64_t shard_stride,
+                 uint32_t n_groups, uint32_t n_heads, uint32_t head_dim, float* out,
+                 uint32_t out_stride, void* stream) {
+    if (!gathered || !out || n_shards == 0 || n_groups == 0 || n_heads == 0 || head_dim == 0)
+        return fail(JX_ERR_INVALID, "bad lse_merge arguments");
+    if (shard_stride < static_cast<uint64_t>(n_groups) * n_heads * (head_dim + 2))
+        return fail(JX_ERR_INVALID, "shard_stride smaller than one shard's partials");
+    if (out_stride < n_heads * head_dim) return fail(JX_ERR_INVALID, "out_stride too small");
+    const int rows = static_cast<int>(n_groups * n_heads);
+    lse_merge_kernel<<<rows, 128, 0, (cudaStream_t)stream>>>(
+        gathered, static_cast<int>(n_shards), static_cast<long long>(shard_stride), rows,
+        static_cast<int>(n_heads), static_cast<int>(head_dim), out, out_stride);
+    JX_CUDA(cudaGetLastError());
+    return JX_OK;
+}
+
+int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream) {
+    if (!kv || !code) return fail(JX_ERR_INVALID, "null argument");
+    DeviceGuard guard(kv->d.device);
+    int h = 0;
+    JX_CUDA(cudaMemcpyAsync(&h, kv->d_err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    JX_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    JX_CUDA(cudaMemsetAsync(kv->d_err, 0, sizeof(int), (cudaStream_t)stream));
+    *code = h;
+    if (h) return fail(JX_ERR_DEVICE, "a kernel reported device error %d (bounded wait ran out)", h);
+    return JX_OK;
+}
+
+int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
+    if (!kv || !key || value < 0) return fail(JX_ERR_INVALID, "bad option");
+    if (!std::strcmp(key, "ctas_per_sm")) kv->opt_ctas_per_sm = value;
+    else if (!std::strcmp(key, "stages")) {
+        if (value == 1 || value > 16) return fail(JX_ERR_INVALID, "stages must be 2..16");
+        kv->opt_stages = value;
+    } else if (!std::strcmp(key, "grid")) kv->opt_grid = value;
+    else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
+    return JX_OK;
+}
+
+int jx_kv_last_launch_count(const jx_kv* kv, int* count) {
+    if (!kv || !count) return fail(JX_ERR_INVALID, "null argument");
+    *count = kv->last_launches;
+    return JX_OK;
+}
+
+int jx_kv_fill_normal(jx_kv* kv, const uint32_t* rows_per_seq, uint64_t seed, void* stream) {
+    if (!kv || !rows_per_seq) return fail(JX_ERR_INVALID, "null argument");
+    for (uint32_t s = 0; s < kv->d.n_seqs; ++s)
+        if (rows_per_seq[s] > kv->d.capacity) return fail(JX_ERR_RANGE, "rows beyond capacity");
+    DeviceGuard guard(kv->d.device);
+    cudaStream_t st = (cudaStream_t)stream;
+    JX_CUDA(cudaMemcpyAsync(kv->d_rows, rows_per_seq, sizeof(uint32_t) * kv->d.n_seqs,
+                            cudaMemcpyHostToDevice, st));
+    const int grid = kv->num_sms * 8;
+    const auto& d = kv->d;
+    if (d.dtype == JX_F32)
+        fill_cache_kernel<DT_F32><<<grid, 256, 0, st>>>(kv->k, kv->v, kv->d_rows, d.n_seqs, d.n_layers,
+                                                        d.capacity, d.row_stride, seed);
+    else if (d.dtype == JX_BF16)
+        fill_cache_kernel<DT_BF16><<<grid, 256, 0, st>>>(kv->k, kv->v, kv->d_rows, d.n_seqs,
+                                                         d.n_layers, d.capacity, d.row_stride, seed);
+    else
+        fill_cache_kernel<DT_F16T><<<grid, 256, 0, st>>>(kv->k, kv->v, kv->d_rows, d.n_seqs,
+                                                         d.n_layers, d.capacity, d.row_stride, seed);
+    JX_CUDA(cudaGetLastError());
+    // the host rows array may be released once this returns
+    JX_CUDA(cudaStreamSynchronize(st));
+    return JX_OK;
+}
+
+int jx_fill_normal_f32(float* dst, uint64_t n, uint64_t seed, uint32_t stream_id, void* stream) {
+    if (!dst) return fail(JX_ERR_INVALID, "null dst");
+    if (n == 0) return JX_OK;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    fill_f32_kernel<<<sms * 8, 256, 0, (cudaStream_t)stream>>>(dst, n, seed, stream_id);
+    JX_CUDA(cudaGetLastError());
+    return JX_OK;
+}
+
+}  // extern "C"

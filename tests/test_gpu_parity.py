@@ -1,0 +1,143 @@
+"""GPU parity: the fused sm_100a step against the CPU oracle on identical seeded inputs.
+
+Bars: KV append bit-exact for every cache type; attention
+output within max-abs 1e-4 of the reference's fp32 CPU attention on an fp32
+cache, and within 2e-2 of it when the cache is bf16.  On identical stored
+bytes the GPU must also agree with the oracle of the same cache type to 1e-4.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle.oracle import BF16, F16T, F32
+from tests.helpers import np_dtype, oracle_step, random_cache
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def run_case(dtype, n_heads, n_kv, hd, lengths, neox=True, n_layers=2, softcap=0.0, window=0,
+             swa_layers=(), grid=0, seed=0, capacity=None, row_pad=0, rope_dim=None,
+             yarn=1.0, rope_freqs=None, check_fp32_ref=False):
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(seed)
+    n_seqs = len(lengths)
+    cap = capacity or max(lengths) + 3
+    rs = n_kv * hd + row_pad
+    rdim = rope_dim or hd
+    layers = [jx.Layer(hd, rdim, 1e6 if l % 2 else 5e5, l, is_swa=l in swa_layers,
+                       rope_freqs=rope_freqs) for l in range(n_layers)]
+    kc = random_cache(rng, (n_seqs, n_layers, cap, rs), dtype)
+    vc = random_cache(rng, (n_seqs, n_layers, cap, rs), dtype)
+    q = rng.standard_normal((n_seqs, n_layers, n_heads * hd)).astype(np.float32)
+    k = rng.standard_normal((n_seqs, n_layers, n_kv * hd)).astype(np.float32)
+    v = rng.standard_normal((n_seqs, n_layers, n_kv * hd)).astype(np.float32)
+    pos = [T - 1 for T in lengths]
+    scale = 1.0 / math.sqrt(hd)
+
+    cache = jx.KVCache(n_seqs, n_layers, cap, rs, dtype)
+    if grid:
+        cache.set_option("grid", grid)
+    for s in range(n_seqs):
+        for l in range(n_layers):
+            cache.write_rows(s, l, 0, 0, kc[s, l])
+            cache.write_rows(s, l, 1, 0, vc[s, l])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    out = torch.full_like(qd, float("nan"))
+    jx.attn_step(cache, layers, qd, kd, vd, out, pos, n_heads, n_kv, scale=scale,
+                 softcap=softcap, sliding_window=window, yarn_scale=yarn, neox=neox)
+    torch.cuda.synchronize()
+    assert cache.check_device_error() == 0
+    got = out.cpu().numpy()
+
+    ko, vo = kc.copy(), vc.copy()
+    ref = oracle_step(ko, vo, dtype, pos, layers, q, k, v, n_heads, n_kv, hd, scale, softcap,
+                      window, yarn, neox, rope_freqs)
+    # appended rows: bit-exact, every other row untouched
+    for s in range(n_seqs):
+        for l in range(n_layers):
+            gk = cache.read_rows(s, l, 0, 0, cap)
+            gv = cache.read_rows(s, l, 1, 0, cap)
+            assert np.array_equal(gk.view(np.uint8), ko[s, l].view(np.uint8)), (s, l, "K")
+            assert np.array_equal(gv.view(np.uint8), vo[s, l].view(np.uint8)), (s, l, "V")
+    err = np.abs(got - ref).max()
+    assert np.isfinite(got).all()
+    assert err <= TOL, f"max-abs {err}"
+    if check_fp32_ref:
+        # the same step on an fp32 cache holding the unrounded values (north-star bf16 bar)
+        kf = kc.astype(np.uint32) << 16 if dtype == BF16 else kc
+        return got, kf
+    cache.close()
+    return got, ref
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16, F16T])
+@pytest.mark.parametrize("neox", [True, False])
+@pytest.mark.parametrize("shape", [(14, 2, 64), (32, 8, 64), (32, 8, 128), (4, 1, 256)])
+def test_step_matches_oracle(dtype, neox, shape):
+    H, HK, hd = shape
+    run_case(dtype, H, HK, hd, [1, 33, 200], neox=neox)
+
+
+@pytest.mark.parametrize("grid", [1, 3, 7, 64])
+def test_split_pieces_merge(grid):
+    # forcing few/many CTAs puts segment boundaries everywhere: multi-piece merges
+    run_case(F32, 32, 8, 64, [5, 97, 300, 1], grid=grid, n_layers=3)
+
+
+@pytest.mark.parametrize("T", [1, 2, 31, 32, 33, 63, 64, 65, 511, 512])
+def test_lengths_tile_edges(T):
+    run_case(F32, 14, 2, 64, [T], n_layers=2)
+
+
+def test_head_dim_32_and_group_8():
+    run_case(F16T, 4, 2, 32, [40, 7])           # toy-model shape (fp16 trunc, native)
+    run_case(BF16, 8, 1, 64, [70])              # group 8
+    run_case(F32, 7, 1, 64, [70])               # group 7 padded to 8
+
+
+def test_softcap_and_window():
+    run_case(F32, 4, 1, 256, [600, 100], softcap=50.0, window=64, swa_layers=(0,), n_layers=3)
+
+
+def test_partial_rope_and_padding():
+    run_case(F32, 8, 2, 128, [50], rope_dim=64, row_pad=32, yarn=2.0)
+    rf = np.linspace(1.0, 8.0, 64).astype(np.float32)
+    run_case(F32, 8, 2, 128, [50], rope_freqs=rf)
+
+
+def test_bf16_cache_within_2e2_of_fp32_reference():
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(5)
+    H, HK, hd, T, L = 32, 8, 64, 700, 2
+    rs = HK * hd
+    kf = rng.standard_normal((1, L, T + 1, rs)).astype(np.float32)
+    vf = rng.standard_normal((1, L, T + 1, rs)).astype(np.float32)
+    q = rng.standard_normal((1, L, H * hd)).astype(np.float32)
+    k = rng.standard_normal((1, L, HK * hd)).astype(np.float32)
+    v = rng.standard_normal((1, L, HK * hd)).astype(np.float32)
+    layers = [jx.Layer(hd, hd, 5e5, l) for l in range(L)]
+    from oracle.oracle import Oracle
+    o = Oracle("port")
+    kb = o.convert_array(kf[0, :, :T - 1], BF16)
+    vb = o.convert_array(vf[0, :, :T - 1], BF16)
+    cache = jx.KVCache(1, L, T + 1, rs, "bf16")
+    for l in range(L):
+        cache.write_rows(0, l, 0, 0, kb[l])
+        cache.write_rows(0, l, 1, 0, vb[l])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    out = torch.zeros_like(qd)
+    jx.attn_step(cache, layers, qd, kd, vd, out, [T - 1], H, HK, neox=False)
+    torch.cuda.synchronize()
+    ref = oracle_step(kf.copy(), vf.copy(), F32, [T - 1], layers, q, k, v, H, HK, hd,
+                      1 / math.sqrt(hd), neox=False)
+    assert np.abs(out.cpu().numpy() - ref).max() <= 2e-2
