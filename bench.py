@@ -1,0 +1,509 @@
+#!/usr/bin/env python
+"""Decode-attention benchmark: KV-read HBM GB/s and steps/s of the fused B200 step.
+
+One step = RoPE + KV append + grouped-query decode attention on every layer of
+every sequence of the workload (jxai src/transformer.cpp:2497-2566).  The
+default workload is Llama-3.2-1B shape (16 layers, 32/8 heads, head_dim 64)
+with an fp32 cache of 4095 rows, appending row 4095.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1..c5] [--dtype f32|bf16]
+    python bench.py --impl reference ...   # the reference's CPU implementation
+
+Multi-GPU (launched by torchrun, one rank per GPU): c1/c2 run one replica per
+GPU; c3/c5 partition the sequences (greedy LPT on length); c4 shards the one
+long sequence by position and merges per-shard (m, l, o) partials after one
+NCCL all-gather.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from jxai_b200 import workloads as W  # noqa: E402
+
+METRIC = "decode-attn KV-read HBM GB/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", default="c2")
+    p.add_argument("--dtype", default=None, help="KV cache type (f32 | bf16 | f16)")
+    p.add_argument("--cpu-sample-s", type=float, default=8.0,
+                   help="seconds of CPU work for the cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--clock-probe-s", type=float, default=1.0,
+                   help="untimed seconds of steps before warm-up so clocks leave idle")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s (earlier measurement on this pool)"
+
+
+def ncu_traffic(key: str):
+    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        e = d.get(key)
+        return None if e is None else float(e["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 100 ms on one GPU."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.dev)], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append((time.time(), ln.strip()))
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            if self.t:
+                self.t.join(timeout=2)
+
+    def summary(self, t0: float, t1: float):
+        rows = []
+        for ts, ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((ts, float(parts[1]), float(parts[2]), parts[4:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        window = [r for r in rows if t0 <= r[0] <= t1] or rows[-5:]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in window:
+            for nm, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(r[1] for r in window),
+                "sm_max_mhz": max(r[2] for r in window), "reasons": sorted(reasons),
+                "samples": len(window)}
+
+
+# ----------------------------------------------------------------------------- our arm
+
+class Runner:
+    """One rank's share of a workload, driven through the public Python API."""
+
+    def __init__(self, w: W.Workload, rank: int, world: int, device: int):
+        import torch
+        import jxai_b200 as jx
+        self.torch, self.jx, self.w = torch, jx, w
+        self.rank, self.world, self.device = rank, world, device
+        self.mode = w.sharding if world > 1 else "replica"
+        T = w.lengths
+        if self.mode == "sequences":
+            self.local = [T[i] for i in W.lpt_partition(T, world)[rank]]
+        else:
+            self.local = list(T)
+        self.pos_base = 0
+        if self.mode == "positions":
+            (b, e) = W.position_shards(T[0], world)[rank]
+            self.pos_base, cap = b, e - b
+            rows = [max(0, min(e, T[0] - 1) - b)]
+        else:
+            cap = max(self.local)
+            rows = [t - 1 for t in self.local]
+        n = len(self.local)
+        self.n = n
+        self.cache = jx.KVCache(n, w.n_layers, cap, w.kv_dim, w.dtype, device, self.pos_base)
+        self.cache.fill_normal(rows, W.SEED + rank)
+        dev = torch.device("cuda", device)
+        self.q = torch.empty(n, w.n_layers, w.q_dim, device=dev)
+        self.k = torch.empty(n, w.n_layers, w.kv_dim, device=dev)
+        self.v = torch.empty_like(self.k)
+        self.out = torch.empty_like(self.q)
+        jx.fill_normal(self.q, W.SEED, 3)
+        jx.fill_normal(self.k, W.SEED, 4)
+        jx.fill_normal(self.v, W.SEED, 5)
+        self.pos = [t - 1 for t in self.local]
+        if self.mode == "positions":
+            hd2 = w.head_dim + 2
+            self.partials = torch.empty(n * w.n_layers * w.n_heads * hd2, device=dev)
+            self.gathered = torch.empty(world * self.partials.numel(), device=dev)
+        # KV bytes this rank reads per step
+        if self.mode == "positions":
+            (b, e) = W.position_shards(T[0], world)[rank]
+            rows_att = sum(max(0, min(e, T[0]) - max(b, T[0] - w.attended(T[0], L)))
+                           for L in w.layers)
+            self.kv_bytes = rows_att * w.kv_dim * 2 * w.elem_size
+        else:
+            self.kv_bytes = w.kv_read_bytes(self.local)
+        self.alg_bytes = self.kv_bytes + w.other_bytes(n)
+
+    def kernel(self, q=None, k=None, v=None, out=None):
+        q = self.q if q is None else q
+        k = self.k if k is None else k
+        v = self.v if v is None else v
+        out = self.out if out is None else out
+        w, jx = self.w, self.jx
+        if self.mode == "positions":
+            jx.attn_step_partial(self.cache, w.layers, q, k, v, self.partials, self.pos,
+                                 w.n_heads, w.n_kv_heads, scale=w.scale,
+                                 sliding_window=w.window, neox=w.neox)
+        else:
+            jx.attn_step(self.cache, w.layers, q, k, v, out, self.pos, w.n_heads, w.n_kv_heads,
+                         scale=w.scale, sliding_window=w.window, neox=w.neox)
+
+    def finish(self, out=None):
+        """Collective tail of a sharded step (all-gather + log-sum-exp merge)."""
+        if self.mode != "positions":
+            return
+        import torch.distributed as dist
+        out = self.out if out is None else out
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.partials)
+            g = self.gathered
+        else:
+            g = self.partials
+        self.jx.lse_merge(g, self.world, self.n * self.w.n_layers, self.w.n_heads,
+                          self.w.head_dim, out, self.w.q_dim)
+
+    def step(self):
+        self.kernel()
+        self.finish()
+
+    def launches_per_step(self):
+        return self.cache.last_launch_count() + (1 if self.mode == "positions" else 0)
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    w = W.make(args.config, args.dtype)
+    r = Runner(w, rank, world, local_rank)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    # untimed clock probe: leave idle clocks before warm-up
+    t_end = time.time() + args.clock_probe_s
+    n_probe = 0
+    while time.time() < t_end:
+        for _ in range(20):
+            r.step()
+        torch.cuda.synchronize()
+        n_probe += 20
+    # every rank must take the same collective steps: agree on the probe count
+    if world > 1:
+        n_probe = int(max_over_ranks(n_probe))
+    for _ in range(args.warmup):
+        r.step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    K = args.steps
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(K)]
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_stop = torch.cuda.Event(enable_timing=True)
+    t_wall0 = time.time()
+    e_start.record(stream)
+    for i in range(K):
+        ev[i][0].record(stream)
+        r.kernel()
+        ev[i][1].record(stream)
+        r.finish()
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    barrier()
+    elapsed_ms = e_start.elapsed_time(e_stop)
+    kernel_ms = sum(a.elapsed_time(b) for a, b in ev) / K
+    err = r.cache.check_device_error()
+    if err:
+        raise RuntimeError(f"device error {err} during the timed region")
+    elapsed_ms = max_over_ranks(elapsed_ms)
+    total_kv = sum_over_ranks(r.kv_bytes)
+    clocks = sampler.summary(t_wall0, t_wall1)
+    sampler.stop()
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        qh = torch.empty(r.q.shape, pin_memory=True)
+        kh = torch.empty(r.k.shape, pin_memory=True)
+        vh = torch.empty(r.v.shape, pin_memory=True)
+        oh = torch.empty(r.out.shape, pin_memory=True)
+        qh.copy_(r.q.cpu()); kh.copy_(r.k.cpu()); vh.copy_(r.v.cpu())
+        qd, kd, vd, od = (torch.empty_like(x) for x in (r.q, r.k, r.v, r.out))
+
+        def e2e_step():
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            r.kernel(qd, kd, vd, od)
+            r.finish(od)
+            oh.copy_(od, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(K):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(a.elapsed_time(b))
+        h2d = sum_over_ranks((qh.numel() + kh.numel() + vh.numel()) * 4)
+        d2h = sum_over_ranks(oh.numel() * 4)
+        e2e = {"value": round(total_kv * K / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+               "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h),
+               "path": "pinned host q/k/v -> H2D -> jx_attn_step (C ABI) -> D2H attn_out"}
+
+    # ---- CPU baseline (rank 0, N=1)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(w, args.cpu_sample_s)
+
+    if rank != 0:
+        return
+    peak, peak_src = peaks()
+    achieved = r.alg_bytes / (kernel_ms * 1e-3) / 1e9
+    traffic = ncu_traffic(f"{w.name}/{w.dtype}") if world == 1 else None
+    steps_per_s = K / (elapsed_ms * 1e-3)
+    value = total_kv * K / (elapsed_ms * 1e-3) / 1e9
+    parallel = {"replica": f"replicas x{world}", "sequences": f"sequences split over {world} GPUs (LPT)",
+                "positions": f"positions sharded over {world} GPUs + NCCL all-gather"}[r.mode]
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_ms / K, 5),
+        "steps_per_s": round(steps_per_s, 2), "higher_is_better": True,
+        "scaling": "weak" if r.mode in ("replica",) else "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-side)",
+        "config": dict(w.describe(), parallelism=parallel,
+                       l2=("inputs larger than L2: %.0f MB of KV per step per GPU > 126 MB" %
+                           (r.kv_bytes / 1e6)) if r.kv_bytes > 126e6 else
+                       "KV per step fits in L2 (latency-bound case)",
+                       kv_bytes_per_step=int(total_kv), clock_probe_steps=n_probe),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "kernel": "jx::decode_kernel", "kernel_ms": round(kernel_ms, 5),
+                     "alg_bytes_per_launch": int(r.alg_bytes), "peak_source": peak_src},
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+        "gpu_launches": int(r.launches_per_step() * K),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- CPU side
+
+def _cpu_oracle():
+    """(Oracle, kind): the reference build when present, else the C restatement."""
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    from oracle.oracle import Oracle, ref_available
+    if ref_available():
+        return Oracle("ref"), "reference"
+    return Oracle("port"), "port"
+
+
+def _cpu_case(w: W.Workload, n_seqs: int, n_layers: int, rng):
+    """Host inputs for n_seqs sequences x n_layers layers of the workload."""
+    from oracle.oracle import BF16, F16T, F32
+    dt = {"f32": F32, "bf16": BF16, "f16": F16T}[w.dtype]
+    lengths = w.lengths[:n_seqs]
+    cap = max(lengths)
+    shape = (n_seqs, n_layers, cap, w.kv_dim)
+    if dt == F32:
+        kc = rng.standard_normal(shape, dtype=np.float32)
+        vc = rng.standard_normal(shape, dtype=np.float32)
+    else:
+        kc = (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        vc = (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    q = rng.standard_normal((n_seqs, n_layers, w.q_dim), dtype=np.float32)
+    k = rng.standard_normal((n_seqs, n_layers, w.kv_dim), dtype=np.float32)
+    v = rng.standard_normal((n_seqs, n_layers, w.kv_dim), dtype=np.float32)
+    layers = [dict(rope_dim=L.rope_dim, rope_base=L.rope_base, is_swa=int(L.is_swa),
+                   shares_kv=0, kv_source_layer=i) for i, L in enumerate(w.layers[:n_layers])]
+    return dt, kc, vc, q, k, v, layers, [t - 1 for t in lengths], lengths
+
+
+def _cpu_sample_shape(w: W.Workload):
+    """Sequences x layers of a bounded CPU sample, and its KV bytes."""
+    n_seqs = min(len(w.lengths), 2 if w.name in ("c3", "c5") else 1)
+    n_layers = w.n_layers if w.name in ("c1", "c2") else min(w.n_layers, 6 if w.name == "c5" else 2)
+    if w.name == "c4":
+        n_layers = 1
+    sub = W.Workload(w.name, w.model, n_layers, w.n_heads, w.n_kv_heads, w.head_dim, w.neox,
+                     w.lengths[:n_seqs], w.dtype, layers=w.layers[:n_layers], window=w.window)
+    return n_seqs, n_layers, sub.kv_read_bytes()
+
+
+def cpu_baseline(w: W.Workload, sample_s: float):
+    orc, kind = _cpu_oracle()
+    n_seqs, n_layers, kv_bytes = _cpu_sample_shape(w)
+    rng = np.random.default_rng(W.SEED)
+    dt, kc, vc, q, k, v, layers, pos, lengths = _cpu_case(w, n_seqs, n_layers, rng)
+    times = []
+    t_end = time.time() + sample_s
+    while True:
+        t0 = time.perf_counter()
+        orc.step(kc, vc, dt, pos, layers, q, k, v, w.n_heads, w.n_kv_heads, w.head_dim, w.scale,
+                 0.0, w.window, 1.0, w.neox)
+        times.append(time.perf_counter() - t0)
+        if time.time() > t_end or len(times) >= 200:
+            break
+    t = statistics.median(times)
+    return {"value": round(kv_bytes / t / 1e9, 3), "unit": "GB/s", "cores": orc.max_threads(),
+            "kind": kind,
+            "sample": f"{n_seqs} seq x {n_layers} layers of {w.name} ({kv_bytes/1e6:.1f} MB KV), "
+                      f"median of {len(times)} runs, {t*1e3:.2f} ms each"}
+
+
+def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the step on this host's cores."""
+    if rank != 0:
+        return
+    w = W.make(args.config, args.dtype)
+    orc, kind = _cpu_oracle()
+    n_seqs, n_layers, kv_bytes = _cpu_sample_shape(w)
+    rng = np.random.default_rng(W.SEED)
+    dt, kc, vc, q, k, v, layers, pos, lengths = _cpu_case(w, n_seqs, n_layers, rng)
+
+    def one():
+        orc.step(kc, vc, dt, pos, layers, q, k, v, w.n_heads, w.n_kv_heads, w.head_dim, w.scale,
+                 0.0, w.window, 1.0, w.neox)
+
+    for _ in range(args.warmup):
+        one()
+    # bound the run to about two minutes: drop layers from the sample if one step is slow
+    t0 = time.perf_counter()
+    one()
+    t1 = time.perf_counter() - t0
+    budget = 120.0 / max(1, args.steps)
+    if t1 > budget and n_layers > 1:
+        n_layers = max(1, int(n_layers * budget / t1))
+        sub = W.Workload(w.name, w.model, n_layers, w.n_heads, w.n_kv_heads, w.head_dim, w.neox,
+                         lengths, w.dtype, layers=w.layers[:n_layers], window=w.window)
+        kv_bytes = sub.kv_read_bytes()
+        dt, kc, vc, q, k, v, layers, pos, lengths = _cpu_case(w, n_seqs, n_layers, rng)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    el = time.perf_counter() - t0
+    value = kv_bytes * args.steps / el / 1e9
+    sample = (f"{n_seqs} seq x {n_layers} layers of {w.name} per step "
+              f"({kv_bytes/1e6:.1f} MB KV); full step = {w.kv_read_bytes()/1e6:.1f} MB")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))", "impl": "reference",
+        "config": dict(w.describe(), parallelism="host CPU, OpenMP over heads"),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": orc.max_threads(),
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+"""The C ABI library: loads, exports every symbol include/jx_attn.h declares,
+matches the header's struct layouts, and fails loudly without a GPU."""
+import ctypes as C
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+import jxai_b200 as jx
+from jxai_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "jx_attn.h")
+
+
+def declared_symbols():
+    with open(HEADER) as fh:
+        text = fh.read()
+    return sorted(set(re.findall(r"JX_API\s+(?:const\s+)?\w+\*?\s+\**(jx_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_binding_list():
+    assert declared_symbols() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = jx.load_library()
+    out = subprocess.run(["nm", "-D", "--defined-only", jx.lib_path()], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    for sym in declared_symbols():
+        assert sym in exported, sym
+        assert getattr(lib, sym) is not None
+    # nothing else leaks out of the C ABI
+    assert {s for s in exported if not s.startswith("jx_")} <= {"_init", "_fini"}
+
+
+def test_version_string():
+    assert b"sm_100a" in jx.load_library().jx_version()
+
+
+def test_struct_layouts_match_header():
+    src = r"""
+#include <stddef.h>
+#include <stdio.h>
+#include "jx_attn.h"
+int main(void) {
+  printf("%zu %zu %zu\n", sizeof(jx_kv_desc), sizeof(jx_layer_desc), sizeof(jx_step_args));
+  printf("%zu %zu %zu %zu\n", offsetof(jx_layer_desc, rope_freqs), offsetof(jx_step_args, q),
+         offsetof(jx_step_args, q_stride), offsetof(jx_step_args, rope_neox));
+  return 0;
+}
+"""
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        with open(c, "w") as fh:
+            fh.write(src)
+        subprocess.run(["gcc", "-I", os.path.dirname(HEADER), c, "-o", exe], check=True)
+        lines = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    sizes = [int(x) for x in lines[0].split()]
+    offs = [int(x) for x in lines[1].split()]
+    assert sizes == [C.sizeof(_lib.KvDesc), C.sizeof(_lib.LayerDesc), C.sizeof(_lib.StepArgs)]
+    assert offs == [_lib.LayerDesc.rope_freqs.offset, _lib.StepArgs.q.offset,
+                    _lib.StepArgs.q_stride.offset, _lib.StepArgs.rope_neox.offset]
+
+
+def test_invalid_arguments_rejected_on_host():
+    lib = jx.load_library()
+    assert lib.jx_kv_create(None, None) == _lib.JX_ERR_INVALID
+    assert b"null" in lib.jx_last_error_string()
+    assert lib.jx_attn_step(None, None, 0, None, None) == _lib.JX_ERR_INVALID
+    assert lib.jx_lse_merge(None, 0, 0, 0, 0, 0, None, 0, None) == _lib.JX_ERR_INVALID
+
+
+def test_no_gpu_means_a_loud_failure():
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(jx.JxError) as e:
+        jx.KVCache(1, 1, 16, 64, "f32")
+    assert e.value.code == _lib.JX_ERR_CUDA

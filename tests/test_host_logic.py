@@ -1,0 +1,46 @@
+"""Host-side logic: workload definitions, byte accounting, partitioning."""
+import numpy as np
+import pytest
+
+from jxai_b200 import workloads as W
+
+
+def test_workload_shapes_and_kv_bytes():
+    # algorithmic KV bytes per step of the benchmark configs (fp32 cache)
+    assert W.make("c1").kv_read_bytes() == 24 * 512 * 128 * 2 * 4
+    assert W.make("c2").kv_read_bytes() == 16 * 4096 * 512 * 8 == 268435456
+    assert W.make("c4").kv_read_bytes() == 32 * 131072 * 1024 * 8
+    c5 = W.make("c5")
+    assert c5.kv_read_bytes() == 64 * (4 * 16384 + 22 * 512) * 256 * 8
+    assert [l for l in range(26) if not c5.layers[l].is_swa] == [5, 11, 17, 23]
+    assert W.make("c3", "bf16").kv_read_bytes() * 2 == W.make("c3").kv_read_bytes()
+
+
+def test_rope_styles_follow_the_reference_arch_table():
+    # src/transformer.cpp:140-179: qwen2/gemma3 Neox, llama (Llama-3.2, Mistral) interleaved
+    assert W.make("c1").neox and W.make("c5").neox
+    assert not W.make("c2").neox and not W.make("c3").neox and not W.make("c4").neox
+
+
+def test_c3_lengths_are_seeded_and_in_range():
+    a, b = W.c3_lengths(), W.c3_lengths()
+    assert a == b and len(a) == 256
+    assert min(a) >= 128 and max(a) <= 8192
+    assert abs(np.mean(a) - 4160) < 400
+
+
+@pytest.mark.parametrize("n", [1, 2, 4, 8])
+def test_lpt_partition_balances_ragged_sequences(n):
+    T = W.c3_lengths()
+    parts = W.lpt_partition(T, n)
+    assert sorted(i for p in parts for i in p) == list(range(256))
+    loads = [sum(T[i] for i in p) for p in parts]
+    assert max(loads) / (sum(T) / n) < 1.01
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 8])
+def test_position_shards_cover_the_sequence(n):
+    sh = W.position_shards(131072, n)
+    assert sh[0][0] == 0 and sh[-1][1] == 131072
+    assert all(a[1] == b[0] for a, b in zip(sh, sh[1:]))
+    assert max(e - b for b, e in sh) - min(e - b for b, e in sh) <= 1
