@@ -95,8 +95,13 @@ def _declare(lib: C.CDLL) -> None:
     lib.jx_version.argtypes = []
 
 
+def checked_build_requested() -> bool:
+    """JXAI_B200_CHECKED=1 selects the diagnostic build with device-side index checks."""
+    return os.environ.get("JXAI_B200_CHECKED", "0") not in ("", "0")
+
+
 def lib_path() -> str:
-    return _build.LIB
+    return _build.LIB_CHECKED if checked_build_requested() else _build.LIB
 
 
 def load(build_if_missing: bool = True) -> C.CDLL:
@@ -105,11 +110,13 @@ def load(build_if_missing: bool = True) -> C.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        if not os.path.exists(_build.LIB) or not _build.up_to_date():
+        checked = checked_build_requested()
+        path = lib_path()
+        if not os.path.exists(path) or not _build.up_to_date(checked):
             if not build_if_missing:
-                raise FileNotFoundError(f"{_build.LIB} is not built")
-            _build.build()
-        lib = C.CDLL(_build.LIB)
+                raise FileNotFoundError(f"{path} is not built")
+            _build.build(checked=checked)
+        lib = C.CDLL(path)
         _declare(lib)
         _lib = lib
         return lib

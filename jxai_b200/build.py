@@ -22,6 +22,10 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libjxattn.so")
 STAMP = os.path.join(BUILD, "libjxattn.sources.sha256")
+# Same sources with every device-side index checked (JX_DEVICE_CHECKS=1): a
+# diagnostic build, selected at load time with JXAI_B200_CHECKED=1.
+LIB_CHECKED = os.path.join(PKG, "libjxattn_checked.so")
+STAMP_CHECKED = os.path.join(BUILD, "checked", "libjxattn.sources.sha256")
 
 SOURCES = ["jx_lib.cu", "jx_decode_f32.cu", "jx_decode_bf16.cu", "jx_decode_f16.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -52,25 +56,32 @@ def sources_digest() -> str:
     return h.hexdigest()
 
 
-def up_to_date() -> bool:
+def up_to_date(checked: bool = False) -> bool:
     """True when the library exists and was built from the current sources."""
-    if not os.path.exists(LIB) or not os.path.exists(STAMP):
+    lib, stamp = (LIB_CHECKED, STAMP_CHECKED) if checked else (LIB, STAMP)
+    if not os.path.exists(lib) or not os.path.exists(stamp):
         return False
-    with open(STAMP) as fh:
+    with open(stamp) as fh:
         return fh.read().strip() == sources_digest()
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False,
+          checked: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
+    lib, stamp = (LIB_CHECKED, STAMP_CHECKED) if checked else (LIB, STAMP)
+    objdir = os.path.join(BUILD, "checked") if checked else BUILD
+    os.makedirs(objdir, exist_ok=True)
     with open(os.path.join(BUILD, ".lock"), "w") as lock:
         fcntl.flock(lock, fcntl.LOCK_EX)  # one builder at a time (e.g. several ranks)
-        if not force and up_to_date():
-            return LIB
+        if not force and up_to_date(checked):
+            return lib
         cc = nvcc()
         extra = ["-Xptxas", "-v"] if ptxas_info else []
+        if checked:
+            extra += ["-DJX_DEVICE_CHECKS=1"]
 
         def compile_one(src: str) -> str:
-            obj = os.path.join(BUILD, src.replace(".cu", ".o"))
+            obj = os.path.join(objdir, src.replace(".cu", ".o"))
             cmd = [cc, *ARCH, *FLAGS, *extra, "-c", os.path.join(CSRC, src), "-o", obj]
             r = subprocess.run(cmd, capture_output=True, text=True)
             if r.returncode != 0:
@@ -82,16 +93,17 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         digest = sources_digest()
         with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
             objs = list(ex.map(compile_one, SOURCES))
-        tmp = f"{LIB}.{os.getpid()}.tmp"
+        tmp = f"{lib}.{os.getpid()}.tmp"
         cmd = [cc, *ARCH, "-shared", "-o", tmp, *objs]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")
-        os.replace(tmp, LIB)
-        with open(STAMP, "w") as fh:
+        os.replace(tmp, lib)
+        with open(stamp, "w") as fh:
             fh.write(digest + "\n")
-        return LIB
+        return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose=True, ptxas_info="--ptxas" in sys.argv,
+                checked="--checked" in sys.argv))

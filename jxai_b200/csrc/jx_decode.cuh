@@ -12,7 +12,10 @@
 //  * Pipeline.  Warp 4 is the producer: it streams 32-row K and V tiles of the
 //    current piece into a ring of shared-memory stages with 4-D TMA tile loads
 //    (128-byte swizzle, no multicast), completion tracked by mbarriers.
-//    Warps 0-3 are consumers; tile k goes to warp k % 4.
+//    Warps 0-3 are consumers; tile k goes to warp k % C with the ring size a
+//    multiple of C, so every use of a given stage is consumed by the same warp,
+//    in order.  (A stage whose successive uses went to different warps could be
+//    waited on two phases ahead, which mbarrier parity cannot tell apart.)
 //  * Math on CUDA cores (the step is HBM-bound: ~2 flop per KV byte at group 4).
 //    QK: lane = cache row, dot product over head_dim in ascending order with
 //    fused multiply-adds (the reference's `dot += q[d]*k[d]` order), q of the
@@ -115,9 +118,19 @@ struct PieceIter {
         i = lo;
     }
 
+    int bad = 0;  // set when the plan is inconsistent (checked builds report it)
+
     __device__ bool next() {
         if (x >= b1) return false;
+        if (JX_DEVICE_CHECKS && (i < 0 || i >= n_pairs)) {
+            bad = 1;
+            return false;
+        }
         pr = pairs[i];
+        if (JX_DEVICE_CHECKS && (pr.len <= 0 || x < pr.off || x >= pr.off + (long long)n_kv * pr.len)) {
+            bad = 2;
+            return false;
+        }
         pi = i;
         const long long rel = x - pr.off;
         kvh = static_cast<int>(rel / pr.len);
@@ -152,6 +165,9 @@ __device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow&
                           static_cast<long long>(pr.cache_layer) * a.layer_stride +
                           static_cast<long long>(pr.append_row) * a.row_stride + kvh * HD;
     const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
+    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && kvh < a.n_kv, 10, pr.io, kvh, 0)) return;
+    if (!JX_CHECKED(a, dst >= 0 && dst + HD <= a.cache_elems, 11, dst, pr.append_row, pr.seq)) return;
+    if (!JX_CHECKED(a, pr.rope_row >= 0 && pr.rope_row < a.n_rope_rows, 12, pr.rope_row, 0, 0)) return;
 #pragma unroll 2
     for (int d = lane; d < HD; d += 32) {
         const float kr = rope_elem(kin, d, pr.rope_half, cs, a.neox != 0);
@@ -165,6 +181,8 @@ __device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow&
 template <int HD>
 __device__ __forceinline__ void emit_final(const DecodeArgs& a, const PairRow& pr, int h, int d,
                                            float M, float L, float O) {
+    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && h < a.n_heads && d < HD, 20, pr.io, h, d))
+        return;
     if (a.part_out) {
         const long long base = (static_cast<long long>(pr.io) * a.n_heads + h) * (HD + 2);
         a.part_out[base + d] = O;
@@ -198,6 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) + 16 * NS <= a.smem_bytes &&
+                           a.n_consumers >= 1 && a.n_consumers <= kConsumerWarps &&
+                           NS % a.n_consumers == 0,
+                    1, a.smem_bytes, NS, a.n_consumers))
+        return;  // every thread takes this branch together
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -228,6 +251,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (it.next()) {
             const PairRow& pr = it.pr;
             const int ntiles = (it.n + kTileRows - 1) / kTileRows;
+            if (!JX_CHECKED(a, it.kvh >= 0 && it.kvh < a.n_kv && pr.cache_layer >= 0 &&
+                                   pr.cache_layer < a.n_cache_layers && pr.seq >= 0 &&
+                                   pr.seq < a.n_cache_seqs && pr.row0 >= 0 &&
+                                   pr.row0 + pr.len <= a.capacity,
+                            30, it.kvh, pr.cache_layer, pr.row0 + pr.len))
+                break;
             int t_app = -1;
             if (pr.append_row >= 0) {
                 const int al = pr.append_row - pr.row0;
@@ -242,32 +271,41 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int stage = tile % NS;
                 const int use = tile / NS;
                 if (use > 0)
-                    mbar_wait_bounded(bars + 8 * (NS + stage), (use - 1) & 1, abort_flag, a.err);
+                    mbar_wait_bounded(bars + 8 * (NS + stage), (use - 1) & 1, abort_flag, a.err,
+                                      a.dbg, 1, tile);
                 const bool issue = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
                 if (!issue) continue;
                 n_issued = tile + 1;
                 if (lane == 0) {
                     const uint32_t fb = bars + 8 * stage;
-                    mbar_arrive_expect_tx(fb, 2 * G::TILEB);
                     const uint32_t dk = base_u32 + stage * 2 * G::TILEB;
                     const uint32_t dv = dk + G::TILEB;
                     const int row = pr.row0 + it.r + t * kTileRows;
+                    if (JX_CHECKED(a, stage >= 0 && stage < NS && row >= 0 && row < a.capacity &&
+                                          (it.kvh + 1) * HD <= a.row_stride,
+                                   31, row, stage, it.kvh)) {
+                        mbar_arrive_expect_tx(fb, 2 * G::TILEB);
 #pragma unroll
-                    for (int b = 0; b < G::NB; ++b) {
-                        const int c0 = it.kvh * HD + b * G::BOXE;
-                        tma_load_4d(dk + b * kTileRows * G::BOX, &tmK, fb, c0, row,
-                                    pr.cache_layer, pr.seq);
-                        tma_load_4d(dv + b * kTileRows * G::BOX, &tmV, fb, c0, row,
-                                    pr.cache_layer, pr.seq);
+                        for (int b = 0; b < G::NB; ++b) {
+                            const int c0 = it.kvh * HD + b * G::BOXE;
+                            tma_load_4d(dk + b * kTileRows * G::BOX, &tmK, fb, c0, row,
+                                        pr.cache_layer, pr.seq);
+                            tma_load_4d(dv + b * kTileRows * G::BOX, &tmV, fb, c0, row,
+                                        pr.cache_layer, pr.seq);
+                        }
+                    } else {
+                        mbar_arrive(fb);  // complete the phase without data
                     }
                 }
                 __syncwarp();
             }
         }
+        JX_CHECKED(a, it.bad == 0, 40 + it.bad, it.x, it.i, b1);
         // Drain: every issued tile load must land before the CTA exits.
         const int first = n_issued > NS ? n_issued - NS : 0;
         for (int k = first; k < n_issued; ++k)
-            mbar_wait_bounded(bars + 8 * (k % NS), (k / NS) & 1, abort_flag, a.err, false);
+            mbar_wait_bounded(bars + 8 * (k % NS), (k / NS) & 1, abort_flag, a.err, a.dbg, 3, k,
+                              false, kDrainLimitCycles);
         return;
     }
 
@@ -299,7 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         // q rotation for this segment's query group -> q_s (padded heads = 0)
         named_bar_sync(1, kConsumerThreads);
-        {
+        if (JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
+                              pr.rope_row < a.n_rope_rows && (kvh + 1) * a.G <= a.n_heads,
+                       50, pr.io, pr.rope_row, kvh)) {
             const float* qin = a.q + static_cast<long long>(pr.io) * a.q_stride +
                                static_cast<long long>(kvh) * a.G * HD;
             const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
@@ -322,9 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
         const int ntiles = (it.n + kTileRows - 1) / kTileRows;
         for (int t = 0; t < ntiles; ++t, ++tile) {
-            if ((tile % kConsumerWarps) != warp) continue;
+            if ((tile % a.n_consumers) != warp) continue;
             const int stage = tile % NS;
-            mbar_wait_bounded(bars + 8 * stage, (tile / NS) & 1, abort_flag, a.err);
+            mbar_wait_bounded(bars + 8 * stage, (tile / NS) & 1, abort_flag, a.err, a.dbg, 2,
+                              tile);
             const int nvalid = min(kTileRows, it.n - t * kTileRows);
             const unsigned char* Kt = base + stage * 2 * G::TILEB;
             const unsigned char* Vt = Kt + G::TILEB;
@@ -489,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (whole) {
                 emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
-            } else {
+            } else if (JX_CHECKED(a, (slot + 1) * GP * (HD + 2) <= a.scratch_floats, 60, slot, seg, 0)) {
                 float* dst = a.scratch + (slot * GP + g) * (HD + 2);
                 dst[d] = O;
                 if (d == 0) {
@@ -504,7 +545,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(1, kConsumerThreads);
             const long long c_first = owner_cta(it.seg_start, a.total, P);
             const long long c_last = owner_cta(it.seg_start + pr.len - 1, a.total, P);
-            if (ctid == 0) {
+            if (ctid == 0 && !JX_CHECKED(a, seg >= 0 && seg < a.n_segments &&
+                                                c_last + seg < P + a.n_segments && c_first >= 0,
+                                         61, seg, c_first, c_last)) {
+                misc[0] = 0;
+            } else if (ctid == 0) {
                 const int prev = atomicAdd(a.counters + seg, 1);
                 const bool last = prev == static_cast<int>(c_last - c_first);
                 misc[0] = last ? 1 : 0;
@@ -513,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             named_bar_sync(1, kConsumerThreads);
             if (misc[0]) {
                 __threadfence();
+                // (slots c_first+seg .. c_last+seg were bounds-checked above)
                 for (int idx = ctid; idx < a.G * HD; idx += kConsumerThreads) {
                     const int g = idx / HD, d = idx % HD;
                     float M = -INFINITY;
@@ -531,6 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
+    JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);
 }
 
 }  // namespace jx

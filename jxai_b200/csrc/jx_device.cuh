@@ -54,29 +54,86 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// A wait that always ends: after `limit_ns` of wall time it raises the CTA's
-// abort flag and the device error word and returns false.  Once the CTA has
-// aborted, later waits return false at once (the caller carries on through
-// its barriers so that no warp is left waiting on another).
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
+// A wait that always ends.  Elapsed time is measured with the SM's own cycle
+// counter (clock64, monotonic per SM) and checked only after a floor of polls,
+// so a jump of the global nanosecond timer cannot end a wait early.  After
+// `limit` cycles the wait raises the CTA's abort flag and the device error
+// word, records where it gave up in dbg[0..7], and returns false.  Once the
+// CTA has aborted, later waits that honour the flag return false at once (the
+// caller carries on through its barriers so no warp waits on another).
+constexpr long long kWaitLimitCycles = 8000000000ll;   // ~4 s at 1.965 GHz
+constexpr long long kDrainLimitCycles = 30000000000ll; // ~15 s: copies in flight at exit
 constexpr int kDevErrWaitTimeout = 1;
+constexpr int kPollFloor = 4096;
+
+__device__ __noinline__ static void report_timeout(int* err, int* dbg, int site, int tile,
+                                                   long long cycles, uint64_t g0) {
+    const uint64_t g1 = global_timer_ns();
+    if (atomicCAS(dbg, 0, 100 + site) == 0) {
+        dbg[1] = static_cast<int>(blockIdx.x);
+        dbg[2] = static_cast<int>(threadIdx.x);
+        dbg[3] = static_cast<int>(cycles);
+        dbg[4] = static_cast<int>(cycles >> 32);
+        dbg[5] = tile;
+        dbg[6] = static_cast<int>((static_cast<long long>(g1 - g0)) / 1000000);  // ms
+        __threadfence();
+    }
+    atomicExch(err, kDevErrWaitTimeout);
+}
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  volatile int* abort_flag, int* err,
-                                                  bool honour_abort = true) {
+                                                  volatile int* abort_flag, int* err, int* dbg,
+                                                  int site, int tile, bool honour_abort = true,
+                                                  long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     if (honour_abort && *abort_flag) return false;
-    const uint64_t t0 = global_timer_ns();
+    const long long c0 = clock64();
+    const uint64_t g0 = global_timer_ns();
+    int polls = 0;
     while (!mbar_try_wait(bar, parity)) {
         if (honour_abort && *abort_flag) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (++polls < kPollFloor) continue;
+        polls = 0;
+        const long long dc = clock64() - c0;
+        if (dc > limit) {
             *abort_flag = 1;
-            atomicExch(err, kDevErrWaitTimeout);
+            report_timeout(err, dbg, site, tile, dc, g0);
             return false;
         }
     }
     return true;
 }
+
+// ---------------------------------------------------------------- optional device checks
+// Built with -DJX_DEVICE_CHECKS=1, every global/shared index and TMA coordinate
+// the decode kernel uses is validated first; a failed check records the first
+// violation in dbg[0..7] (code, block, three values), raises the device error
+// word, and the access is skipped -- nothing traps.
+#ifndef JX_DEVICE_CHECKS
+#define JX_DEVICE_CHECKS 0
+#endif
+constexpr int kDevErrCheck = 2;
+
+static __device__ __noinline__ void report_check(int* err, int* dbg, int code, long long v0, long long v1,
+                                          long long v2) {
+    if (atomicCAS(dbg, 0, code) == 0) {
+        dbg[1] = static_cast<int>(blockIdx.x);
+        dbg[2] = static_cast<int>(threadIdx.x);
+        dbg[3] = static_cast<int>(v0);
+        dbg[4] = static_cast<int>(v0 >> 32);
+        dbg[5] = static_cast<int>(v1);
+        dbg[6] = static_cast<int>(v2);
+        __threadfence();
+    }
+    atomicExch(err, kDevErrCheck);
+}
+
+// `ok` evaluates to the condition; on failure the violation is reported.
+#define JX_CHECKED(args, cond, code, v0, v1, v2)                                  \
+    ((!JX_DEVICE_CHECKS) || (cond) ||                                             \
+     (::jx::report_check((args).err, (args).dbg, (code), (long long)(v0),         \
+                         (long long)(v1), (long long)(v2)),                       \
+      false))
 
 // ---------------------------------------------------------------- TMA
 // Tiled 4-D load global -> this CTA's shared memory, completion counted on an

@@ -53,6 +53,18 @@ struct DecodeArgs {
     float* part_out; // partial mode output, or null
     int* err;        // device error word
     int n_stages;
+    int n_consumers; // consumer warps that take tiles (1..4); n_stages % n_consumers == 0
+    // extents, used by the optional device-side checks (JX_DEVICE_CHECKS builds)
+    long long n_io;          // rows of q/k/v/out
+    long long cache_elems;   // elements of K (and of V)
+    long long scratch_floats;
+    long long n_segments;
+    int n_rope_rows;
+    int capacity;
+    int n_cache_layers;
+    int n_cache_seqs;
+    int smem_bytes;          // dynamic shared memory of the launch
+    int* dbg;                // [8]: first failed check (code, block, values)
 };
 
 // Host-side launch request for one fused decode launch.

@@ -198,6 +198,7 @@ struct jx_kv {
     std::vector<uint32_t> seq_pos;
     int num_sms = 0;
     int* d_err = nullptr;
+    int* d_dbg = nullptr;        // [8] first failed device check (checked builds)
     uint32_t* d_rows = nullptr;  // fill helper
     float* d_scratch = nullptr;
     size_t scratch_floats = 0;
@@ -239,22 +240,30 @@ int encode_maps(jx_kv* kv, int box_kind) {
     return JX_OK;
 }
 
-// Default pipeline depth / residency for one kernel configuration: the
-// deepest ring (<= 8 stages) that still lets two CTAs share an SM, else one
-// CTA with the deepest ring that fits.
+// Consumer warps that take tiles for a ring of `stages`: every stage must be
+// consumed by one warp only, so the count divides the ring size.
+int consumers_for(int stages) {
+    for (int c = 4; c > 1; --c)
+        if (stages % c == 0) return c;
+    return 1;
+}
+
+// Default pipeline depth / residency for one kernel configuration: a ring of
+// 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if it
+// fits, else with one CTA per SM, else the deepest ring that fits one CTA.
 void default_shape(int hd, int gp, int dtype, int* stages, int* cps) {
     const int per_sm = 227 * 1024;
-    int best = 0;
-    for (int ns = 8; ns >= 2; --ns)
-        if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 <= per_sm / 2) { best = ns; break; }
-    if (best) {
-        *stages = best;
-        *cps = 2;
-        return;
-    }
-    for (int ns = 8; ns >= 2; --ns)
+    for (int c = 2; c >= 1; --c)
+        for (int ns : {8, 4})
+            if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
+                *stages = ns;
+                *cps = c;
+                return;
+            }
+    int best = 2;
+    for (int ns = 7; ns >= 2; --ns)
         if (decode_smem_bytes(hd, gp, dtype, ns) <= per_sm) { best = ns; break; }
-    *stages = best ? best : 2;
+    *stages = best;
     *cps = 1;
 }
 
@@ -498,6 +507,23 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
             }
         }
         const long long total = off;
+        // The kernel trusts the plan: validate every row of it here.
+        {
+            long long o = 0;
+            for (const PairRow& pr : pairs) {
+                const bool ok = pr.off == o && pr.len >= 0 && pr.row0 >= 0 &&
+                                static_cast<long long>(pr.row0) + pr.len <= D.capacity &&
+                                (pr.append_row < 0 ||
+                                 (pr.append_row >= pr.row0 && pr.append_row < pr.row0 + pr.len)) &&
+                                pr.rope_row >= 0 && pr.rope_row < static_cast<int>(rope_ids.size()) &&
+                                pr.io >= 0 && pr.io < static_cast<int>(a->n_seqs * n_layers) &&
+                                pr.cache_layer >= 0 && pr.cache_layer < static_cast<int>(D.n_layers) &&
+                                pr.seq >= 0 && pr.seq < static_cast<int>(D.n_seqs) &&
+                                pr.rope_half >= 0 && pr.rope_half <= hd / 2;
+                if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent work plan row");
+                o += static_cast<long long>(pr.len) * a->n_kv_heads;
+            }
+        }
         const size_t pair_bytes = pairs.size() * sizeof(PairRow);
         const size_t rope_off = (pair_bytes + 255) & ~static_cast<size_t>(255);
         std::vector<unsigned char> bytes(rope_off + rope.size() * sizeof(float2), 0);
@@ -565,6 +591,17 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.part_out = partial ? partials : nullptr;
         A.err = kv->d_err;
         A.n_stages = stages;
+        A.n_consumers = consumers_for(stages);
+        A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
+        A.cache_elems = kv->seq_stride * D.n_seqs;
+        A.scratch_floats = static_cast<long long>(kv->scratch_floats);
+        A.n_segments = n_segs;
+        A.n_rope_rows = static_cast<int>(rope_ids.size());
+        A.capacity = static_cast<int>(D.capacity);
+        A.n_cache_layers = static_cast<int>(D.n_layers);
+        A.n_cache_seqs = static_cast<int>(D.n_seqs);
+        A.smem_bytes = decode_smem_bytes(hd, gp, D.dtype, stages);
+        A.dbg = kv->d_dbg;
         Lc.tmK = &kv->tmK[box_kind];
         Lc.tmV = &kv->tmV[box_kind];
         Lc.head_dim = hd;
@@ -635,6 +672,8 @@ int jx_kv_create(const jx_kv_desc* desc, jx_kv** out) {
     if (cudaMemset(kv->k, 0, bytes) != cudaSuccess || cudaMemset(kv->v, 0, bytes) != cudaSuccess ||
         cudaMalloc(&kv->d_err, sizeof(int)) != cudaSuccess ||
         cudaMemset(kv->d_err, 0, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&kv->d_dbg, 8 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(kv->d_dbg, 0, 8 * sizeof(int)) != cudaSuccess ||
         cudaMalloc(&kv->d_rows, sizeof(uint32_t) * d.n_seqs) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess)
         return cleanup(fail(JX_ERR_CUDA, "cache initialisation failed"));
@@ -649,6 +688,7 @@ int jx_kv_destroy(jx_kv* kv) {
     cudaFree(kv->k);
     cudaFree(kv->v);
     cudaFree(kv->d_err);
+    cudaFree(kv->d_dbg);
     cudaFree(kv->d_rows);
     cudaFree(kv->d_scratch);
     cudaFree(kv->d_counters);
@@ -794,12 +834,30 @@ int jx_lse_merge(const float* gathered, uint32_t n_shards, uint64_t shard_stride
 int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream) {
     if (!kv || !code) return fail(JX_ERR_INVALID, "null argument");
     DeviceGuard guard(kv->d.device);
-    int h = 0;
-    JX_CUDA(cudaMemcpyAsync(&h, kv->d_err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
-    JX_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
-    JX_CUDA(cudaMemsetAsync(kv->d_err, 0, sizeof(int), (cudaStream_t)stream));
+    int h = 0, dbg[8] = {0};
+    cudaStream_t st = (cudaStream_t)stream;
+    JX_CUDA(cudaMemcpyAsync(&h, kv->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    JX_CUDA(cudaMemcpyAsync(dbg, kv->d_dbg, sizeof dbg, cudaMemcpyDeviceToHost, st));
+    JX_CUDA(cudaStreamSynchronize(st));
+    JX_CUDA(cudaMemsetAsync(kv->d_err, 0, sizeof(int), st));
+    JX_CUDA(cudaMemsetAsync(kv->d_dbg, 0, sizeof dbg, st));
+    JX_CUDA(cudaStreamSynchronize(st));
     *code = h;
-    if (h) return fail(JX_ERR_DEVICE, "a kernel reported device error %d (bounded wait ran out)", h);
+    if (h == kDevErrWaitTimeout)
+        return fail(JX_ERR_DEVICE,
+                    "a decode kernel's bounded wait ran out: site %d block %d thread %d tile %d "
+                    "after %lld cycles (%d ms of global timer)",
+                    dbg[0] - 100, dbg[1], dbg[2], dbg[5],
+                    static_cast<long long>((static_cast<uint64_t>(static_cast<uint32_t>(dbg[4])) << 32) |
+                                           static_cast<uint32_t>(dbg[3])),
+                    dbg[6]);
+    if (h)
+        return fail(JX_ERR_DEVICE,
+                    "device check %d failed in block %d thread %d: values %lld %d %d (error %d)",
+                    dbg[0], dbg[1], dbg[2],
+                    static_cast<long long>((static_cast<uint64_t>(static_cast<uint32_t>(dbg[4])) << 32) |
+                                           static_cast<uint32_t>(dbg[3])),
+                    dbg[5], dbg[6], h);
     return JX_OK;
 }
 

@@ -141,3 +141,65 @@ def test_bf16_cache_within_2e2_of_fp32_reference():
     ref = oracle_step(kf.copy(), vf.copy(), F32, [T - 1], layers, q, k, v, H, HK, hd,
                       1 / math.sqrt(hd), neox=False)
     assert np.abs(out.cpu().numpy() - ref).max() <= 2e-2
+
+
+@pytest.mark.parametrize("stages", [2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("grid", [1, 3])
+def test_every_ring_size_on_long_pieces(stages, grid):
+    # one or three CTAs walk thousands of rows: every stage is reused many
+    # times, so a consumer that could wait on the wrong phase would show up
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(stages * 10 + grid)
+    H, HK, hd, T = 8, 2, 64, 3000
+    rs = HK * hd
+    kc = rng.standard_normal((1, 1, T + 1, rs)).astype(np.float32)
+    vc = rng.standard_normal((1, 1, T + 1, rs)).astype(np.float32)
+    q = rng.standard_normal((1, 1, H * hd)).astype(np.float32)
+    k = rng.standard_normal((1, 1, HK * hd)).astype(np.float32)
+    v = rng.standard_normal((1, 1, HK * hd)).astype(np.float32)
+    layers = [jx.Layer(hd, hd, 5e5, 0)]
+    cache = jx.KVCache(1, 1, T + 1, rs, "f32")
+    cache.set_option("stages", stages)
+    cache.set_option("grid", grid)
+    cache.write_rows(0, 0, 0, 0, kc[0, 0])
+    cache.write_rows(0, 0, 1, 0, vc[0, 0])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    ref = oracle_step(kc.copy(), vc.copy(), F32, [T - 1], layers, q, k, v, H, HK, hd,
+                      1 / math.sqrt(hd), neox=False)
+    for _ in range(3):
+        out = torch.full_like(qd, float("nan"))
+        jx.attn_step(cache, layers, qd, kd, vd, out, [T - 1], H, HK, neox=False)
+        torch.cuda.synchronize()
+        assert cache.check_device_error() == 0
+        assert np.abs(out.cpu().numpy() - ref).max() <= TOL
+    cache.close()
+
+
+@pytest.mark.parametrize("hd,stages", [(128, 2), (128, 3), (128, 4), (256, 2), (256, 3)])
+def test_wide_heads_long_pieces(hd, stages):
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(hd + stages)
+    H, HK, T = 8, 2, 1500
+    rs = HK * hd
+    kc = rng.standard_normal((1, 1, T + 1, rs)).astype(np.float32)
+    vc = rng.standard_normal((1, 1, T + 1, rs)).astype(np.float32)
+    q = rng.standard_normal((1, 1, H * hd)).astype(np.float32)
+    k = rng.standard_normal((1, 1, HK * hd)).astype(np.float32)
+    v = rng.standard_normal((1, 1, HK * hd)).astype(np.float32)
+    layers = [jx.Layer(hd, hd, 1e6, 0)]
+    cache = jx.KVCache(1, 1, T + 1, rs, "f32")
+    cache.set_option("stages", stages)
+    cache.set_option("grid", 2)
+    cache.write_rows(0, 0, 0, 0, kc[0, 0])
+    cache.write_rows(0, 0, 1, 0, vc[0, 0])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    out = torch.zeros_like(qd)
+    jx.attn_step(cache, layers, qd, kd, vd, out, [T - 1], H, HK, neox=True)
+    torch.cuda.synchronize()
+    assert cache.check_device_error() == 0
+    ref = oracle_step(kc.copy(), vc.copy(), F32, [T - 1], layers, q, k, v, H, HK, hd,
+                      1 / math.sqrt(hd), neox=True)
+    assert np.abs(out.cpu().numpy() - ref).max() <= TOL
+    cache.close()
