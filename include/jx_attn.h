@@ -161,6 +161,24 @@ JX_API int jx_lse_merge(const float* gathered, uint32_t n_shards, uint64_t shard
                  uint32_t n_groups, uint32_t n_heads, uint32_t head_dim, float* out,
                  uint32_t out_stride, void* stream);
 
+/* The same step as jx_attn_step for callers that cannot allocate GPU memory.
+ * No counterpart in the reference (its cache lives in host vectors).  For an
+ * engine that gives all of HBM to its own arena or pool, or a serving loop
+ * that must not run into cudaMalloc/cudaFree (and their implicit device
+ * synchronisation) mid-token: the caller passes the K and V caches as its own
+ * device buffers laid out as jx_kv_create lays them out ([n_seqs][n_layers]
+ * [capacity][row_stride] of desc->dtype; desc->device must be current), and
+ * the call allocates nothing -- its scratch (split partials, arrival
+ * counters, work plan) is one fixed 8 MiB array per GPU, reserved while the
+ * library is loaded.  Steps needing more scratch are rejected with
+ * JX_ERR_RANGE.  All calls share that array: calls that overlap on the GPU
+ * race.  The first call on a device looks up the array's address; make it
+ * before any stream capture.  All layers of one call share head_dim, and no
+ * shares_kv layer may read a cache layer appended in the same call. */
+JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache, void* v_cache,
+                                const jx_layer_desc* layers, uint32_t n_layers,
+                                const jx_step_args* args, void* stream);
+
 /* ---- diagnostics, tuning, harness helpers --------------------------------- */
 
 /* Reads and clears the handle's device error word (synchronises the stream).

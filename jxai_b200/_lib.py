@@ -28,6 +28,7 @@ EXPORTS = (
     "jx_kv_layer_ptr", "jx_attn_step", "jx_attn_step_partial", "jx_lse_merge",
     "jx_kv_check_device_error", "jx_kv_set_option", "jx_kv_last_launch_count",
     "jx_kv_fill_normal", "jx_fill_normal_f32", "jx_last_error_string", "jx_version",
+    "jx_attn_step_noalloc",
 )
 
 
@@ -84,6 +85,8 @@ def _declare(lib: C.CDLL) -> None:
         "jx_kv_last_launch_count": [vp, C.POINTER(C.c_int)],
         "jx_kv_fill_normal": [vp, C.POINTER(u32), u64, vp],
         "jx_fill_normal_f32": [vp, u64, u64, u32, vp],
+        "jx_attn_step_noalloc": [C.POINTER(KvDesc), vp, vp, C.POINTER(LayerDesc), u32,
+                                 C.POINTER(StepArgs), vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

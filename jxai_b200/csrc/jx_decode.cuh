@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
             }
         }
-        JX_CHECKED(a, it.bad == 0, 40 + it.bad, it.x, it.i, b1);
+        (void)JX_CHECKED(a, it.bad == 0, 40 + it.bad, it.x, it.i, b1);
         // Drain: every issued tile load must land before the CTA exits.
         const int first = n_issued > NS ? n_issued - NS : 0;
         for (int k = first; k < n_issued; ++k)
@@ -577,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);
+    (void)JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);
 }
 
 }  // namespace jx

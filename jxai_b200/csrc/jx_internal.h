@@ -87,5 +87,15 @@ int decode_smem_bytes(int head_dim, int gp, int dtype, int stages);
 int decode_ctas_per_sm(int head_dim, int gp, int dtype, int stages);
 // Launches; returns a cudaError_t.
 cudaError_t decode_launch(const DecodeLaunch& L);
+// Consumer warps for a ring of `stages` (a divisor of it, at most 4).
+int consumers_for(int stages);
+// Default ring depth and CTAs per SM for one kernel configuration.
+void default_shape(int hd, int gp, int dtype, int* stages, int* cps);
+// Sets the calling thread's jx_last_error_string() message.
+void set_last_error(const char* msg);
+// (cos, sin) of every rotated pair at `pos`, as apply_rope computes them;
+// writes `width` entries (zeros past the rotated pairs).
+void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
+              bool neox, const float* rope_freqs, float2* out, int width);
 
 }  // namespace jx

@@ -118,6 +118,55 @@ __global__ void fill_f32_kernel(float* dst, uint64_t n, uint64_t seed, uint32_t 
         dst[i] = normal_at(seed, stream_id, i);
 }
 
+// Consumer warps that take tiles for a ring of `stages`: every stage must be
+// consumed by one warp only, so the count divides the ring size.
+int consumers_for(int stages) {
+    for (int c = 4; c > 1; --c)
+        if (stages % c == 0) return c;
+    return 1;
+}
+
+// Default pipeline depth / residency for one kernel configuration: a ring of
+// 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if it
+// fits, else with one CTA per SM, else the deepest ring that fits one CTA.
+void default_shape(int hd, int gp, int dtype, int* stages, int* cps) {
+    const int per_sm = 227 * 1024;
+    for (int c = 2; c >= 1; --c)
+        for (int ns : {8, 4})
+            if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
+                *stages = ns;
+                *cps = c;
+                return;
+            }
+    int best = 2;
+    for (int ns = 7; ns >= 2; --ns)
+        if (decode_smem_bytes(hd, gp, dtype, ns) <= per_sm) { best = ns; break; }
+    *stages = best;
+    *cps = 1;
+}
+
+// (cos, sin) of every rotated pair at `pos`, computed with the same float
+// expressions as apply_rope (src/transformer.cpp:82-92, 112-116).
+void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
+              bool neox, const float* rope_freqs, float2* out, int width) {
+    const uint32_t rdim = std::min(head_dim, rope_dim);
+    const float pos_scaled = static_cast<float>(pos) / std::max(1e-4f, yarn_scale);
+    const uint32_t half = rdim / 2;
+    for (int j = 0; j < width; ++j) out[j] = make_float2(0.0f, 0.0f);
+    for (uint32_t j = 0; j < half; ++j) {
+        float freq;
+        if (neox) {
+            freq = 1.0f / std::pow(base, (2.0f * static_cast<float>(j)) / static_cast<float>(rdim));
+            if (rope_freqs) freq /= rope_freqs[j];
+        } else {
+            const uint32_t d = 2 * j;
+            freq = 1.0f / std::pow(base, static_cast<float>(d) / static_cast<float>(rdim));
+        }
+        const float angle = pos_scaled * freq;
+        out[j] = make_float2(std::cos(angle), std::sin(angle));
+    }
+}
+
 }  // namespace jx
 
 using namespace jx;
@@ -136,6 +185,8 @@ static int fail(int code, const char* fmt, ...) {
     g_err = buf;
     return code;
 }
+
+void jx::set_last_error(const char* msg) { g_err = msg; }
 
 #define JX_CUDA(call)                                                                    \
     do {                                                                                 \
@@ -240,33 +291,6 @@ int encode_maps(jx_kv* kv, int box_kind) {
     return JX_OK;
 }
 
-// Consumer warps that take tiles for a ring of `stages`: every stage must be
-// consumed by one warp only, so the count divides the ring size.
-int consumers_for(int stages) {
-    for (int c = 4; c > 1; --c)
-        if (stages % c == 0) return c;
-    return 1;
-}
-
-// Default pipeline depth / residency for one kernel configuration: a ring of
-// 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if it
-// fits, else with one CTA per SM, else the deepest ring that fits one CTA.
-void default_shape(int hd, int gp, int dtype, int* stages, int* cps) {
-    const int per_sm = 227 * 1024;
-    for (int c = 2; c >= 1; --c)
-        for (int ns : {8, 4})
-            if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
-                *stages = ns;
-                *cps = c;
-                return;
-            }
-    int best = 2;
-    for (int ns = 7; ns >= 2; --ns)
-        if (decode_smem_bytes(hd, gp, dtype, ns) <= per_sm) { best = ns; break; }
-    *stages = best;
-    *cps = 1;
-}
-
 int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& bytes,
                 cudaStream_t stream) {
     if (kv->slots.size() <= slot_i) kv->slots.resize(slot_i + 1);
@@ -322,28 +346,6 @@ int ensure_scratch(jx_kv* kv, size_t floats, size_t counters) {
         kv->counters_n = counters;
     }
     return JX_OK;
-}
-
-// (cos, sin) of every rotated pair at `pos`, computed with the same float
-// expressions as apply_rope (src/transformer.cpp:82-92, 112-116).
-void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
-              bool neox, const float* rope_freqs, float2* out, int width) {
-    const uint32_t rdim = std::min(head_dim, rope_dim);
-    const float pos_scaled = static_cast<float>(pos) / std::max(1e-4f, yarn_scale);
-    const uint32_t half = rdim / 2;
-    for (int j = 0; j < width; ++j) out[j] = make_float2(0.0f, 0.0f);
-    for (uint32_t j = 0; j < half; ++j) {
-        float freq;
-        if (neox) {
-            freq = 1.0f / std::pow(base, (2.0f * static_cast<float>(j)) / static_cast<float>(rdim));
-            if (rope_freqs) freq /= rope_freqs[j];
-        } else {
-            const uint32_t d = 2 * j;
-            freq = 1.0f / std::pow(base, static_cast<float>(d) / static_cast<float>(rdim));
-        }
-        const float angle = pos_scaled * freq;
-        out[j] = make_float2(std::cos(angle), std::sin(angle));
-    }
 }
 
 uint64_t hash_floats(const float* p, size_t n) {
