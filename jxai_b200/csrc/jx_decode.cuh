@@ -103,12 +103,17 @@ struct PieceIter {
     int pi, kvh, r, n;
     long long seg_start;
 
-    __device__ void init(const PairRow* p, int np, int nkv, long long b0_, long long b1_) {
+    __device__ void init(const PairRow* p, int np, int nkv, long long b0_, long long b1_,
+                         const int* start_hint) {
         pairs = p;
         n_pairs = np;
         n_kv = nkv;
         x = b0_;
         b1 = b1_;
+        if (start_hint) {  // precomputed by the host for this CTA
+            i = start_hint[blockIdx.x];
+            return;
+        }
         // largest i with pairs[i].off <= x (zero-length pairs share the next offset)
         int lo = 0, hi = np - 1;
         while (lo < hi) {
@@ -245,8 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             prefetch_tensormap(&tmV);
         }
         PieceIter it;
-        it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1);
+        it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1, a.cta_pair);
         int tile = 0;
+        int stage = 0;         // tile % NS
+        uint32_t phase = 0;    // (tile / NS) & 1
         int n_issued = 0;  // tiles [0, n_issued) had their loads issued
         while (it.next()) {
             const PairRow& pr = it.pr;
@@ -268,22 +275,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     fence_proxy_async_global();
                     __syncwarp();
                 }
-                const int stage = tile % NS;
-                const int use = tile / NS;
-                if (use > 0)
-                    mbar_wait_bounded(bars + 8 * (NS + stage), (use - 1) & 1, abort_flag, a.err,
-                                      a.dbg, 1, tile);
+                const int cur_stage = stage;
+                const uint32_t cur_phase = phase;
+                if (++stage == NS) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+                // wait until the previous use of this stage (tile - NS) has been released
+                if (tile >= NS)
+                    mbar_wait_bounded(bars + 8 * (NS + cur_stage), cur_phase ^ 1u, abort_flag,
+                                      a.err, a.dbg, 1, tile);
                 const bool issue = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
                 if (!issue) continue;
                 n_issued = tile + 1;
+                const int stage_ = cur_stage;
                 if (lane == 0) {
-                    const uint32_t fb = bars + 8 * stage;
-                    const uint32_t dk = base_u32 + stage * 2 * G::TILEB;
+                    const uint32_t fb = bars + 8 * stage_;
+                    const uint32_t dk = base_u32 + stage_ * 2 * G::TILEB;
                     const uint32_t dv = dk + G::TILEB;
                     const int row = pr.row0 + it.r + t * kTileRows;
-                    if (JX_CHECKED(a, stage >= 0 && stage < NS && row >= 0 && row < a.capacity &&
+                    if (JX_CHECKED(a, stage_ >= 0 && stage_ < NS && row >= 0 && row < a.capacity &&
                                           (it.kvh + 1) * HD <= a.row_stride,
-                                   31, row, stage, it.kvh)) {
+                                   31, row, stage_, it.kvh)) {
                         mbar_arrive_expect_tx(fb, 2 * G::TILEB);
 #pragma unroll
                         for (int b = 0; b < G::NB; ++b) {
@@ -326,8 +339,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     PieceIter it;
-    it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1);
-    int tile = 0;
+    it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1, a.cta_pair);
+    const int C = a.n_consumers;
+    const bool active = warp < C;
+    int tile_base = 0;          // global index of the current piece's first tile
+    int my_k = warp;            // this warp's next tile (global index)
+    int my_stage = warp;        // my_k % NS
+    uint32_t my_phase = 0;      // (my_k / NS) & 1
     const float scale = a.scale;
     const float softcap = a.softcap;
     const float inv_cap = a.inv_softcap;
@@ -361,13 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 
         const int ntiles = (it.n + kTileRows - 1) / kTileRows;
-        for (int t = 0; t < ntiles; ++t, ++tile) {
-            if ((tile % a.n_consumers) != warp) continue;
-            const int stage = tile % NS;
-            mbar_wait_bounded(bars + 8 * stage, (tile / NS) & 1, abort_flag, a.err, a.dbg, 2,
-                              tile);
+        const int tile_end = tile_base + ntiles;
+        // this warp's tiles of the piece: my_k, my_k + C, ... (stage and phase tracked
+        // incrementally; the ring size is a multiple of C)
+        while (active && my_k < tile_end) {
+            const int t = my_k - tile_base;
+            mbar_wait_bounded(bars + 8 * my_stage, my_phase, abort_flag, a.err, a.dbg, 2, my_k);
             const int nvalid = min(kTileRows, it.n - t * kTileRows);
-            const unsigned char* Kt = base + stage * 2 * G::TILEB;
+            const unsigned char* Kt = base + my_stage * 2 * G::TILEB;
             const unsigned char* Vt = Kt + G::TILEB;
 
             // ---- scores: lane = row
@@ -433,8 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
 
             // ---- PV: lane = head dims [lane*DPL, lane*DPL + DPL)
-#pragma unroll 2
-            for (int rr = 0; rr < nvalid; ++rr) {
+            auto pv_row = [&](const int rr) {
                 float pr_[GP];
                 if constexpr (GP % 4 == 0) {
 #pragma unroll
@@ -491,10 +509,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int g = 0; g < GP; ++g)
 #pragma unroll
                     for (int k = 0; k < G::DPL; ++k) o[g][k] = __fmaf_rn(pr_[g], vv[k], o[g][k]);
+            
+            };
+            if (nvalid == kTileRows) {
+#pragma unroll
+                for (int rr = 0; rr < kTileRows; ++rr) pv_row(rr);
+            } else {
+#pragma unroll 2
+                for (int rr = 0; rr < nvalid; ++rr) pv_row(rr);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(bars + 8 * (NS + stage));
+            if (lane == 0) mbar_arrive(bars + 8 * (NS + my_stage));
+            my_k += C;
+            my_stage += C;
+            if (my_stage >= NS) {
+                my_stage -= NS;
+                my_phase ^= 1u;
+            }
         }
+        tile_base = tile_end;
 
         // ---- merge the four warps' states for this piece
 #pragma unroll

@@ -27,6 +27,7 @@ static_assert(sizeof(PairRow) == 48, "PairRow layout");
 
 struct DecodeArgs {
     const PairRow* pairs;
+    const int* cta_pair;  // per CTA: the pair holding its first row (or null: binary search)
     int n_pairs;
     int n_kv;       // kv heads
     int G;          // query heads per kv head

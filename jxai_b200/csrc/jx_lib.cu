@@ -526,14 +526,6 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 o += static_cast<long long>(pr.len) * a->n_kv_heads;
             }
         }
-        const size_t pair_bytes = pairs.size() * sizeof(PairRow);
-        const size_t rope_off = (pair_bytes + 255) & ~static_cast<size_t>(255);
-        std::vector<unsigned char> bytes(rope_off + rope.size() * sizeof(float2), 0);
-        std::memcpy(bytes.data(), pairs.data(), pair_bytes);
-        if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope.size() * sizeof(float2));
-        rc = upload_plan(kv, gi, bytes, stream);
-        if (rc) return rc;
-
         // ---- launch shape (cached per configuration)
         int stages = 0, cps = 0;
         const auto skey = std::make_tuple(hd, gp, kv->opt_stages, kv->opt_ctas_per_sm);
@@ -558,6 +550,27 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         P = std::min<long long>(P, std::max<long long>(1, (total + 63) / 64));
         if (kv->opt_grid) P = kv->opt_grid;
         if (total == 0) P = 1;
+        // each CTA's first pair (the kernel then needs no search to find its slice)
+        std::vector<int> cta_pair(static_cast<size_t>(P), 0);
+        for (long long c = 0; c < P; ++c) {
+            const long long x = total * c / P;
+            int lo = 0, hi = static_cast<int>(pairs.size()) - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (pairs[mid].off <= x) lo = mid; else hi = mid - 1;
+            }
+            cta_pair[c] = lo;
+        }
+        const size_t pair_bytes = pairs.size() * sizeof(PairRow);
+        const size_t rope_off = (pair_bytes + 255) & ~static_cast<size_t>(255);
+        const size_t rope_bytes = rope.size() * sizeof(float2);
+        const size_t cta_off = (rope_off + rope_bytes + 255) & ~static_cast<size_t>(255);
+        std::vector<unsigned char> bytes(cta_off + cta_pair.size() * sizeof(int), 0);
+        std::memcpy(bytes.data(), pairs.data(), pair_bytes);
+        if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope_bytes);
+        std::memcpy(bytes.data() + cta_off, cta_pair.data(), cta_pair.size() * sizeof(int));
+        rc = upload_plan(kv, gi, bytes, stream);
+        if (rc) return rc;
         const long long n_segs = static_cast<long long>(pairs.size()) * a->n_kv_heads;
         rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * (hd + 2),
                             static_cast<size_t>(std::max<long long>(n_segs, 1)));
@@ -566,6 +579,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         DecodeLaunch Lc{};
         DecodeArgs& A = Lc.args;
         A.pairs = static_cast<const PairRow*>(kv->slots[gi].d_buf);
+        A.cta_pair = reinterpret_cast<const int*>(static_cast<unsigned char*>(kv->slots[gi].d_buf) +
+                                                  cta_off);
         A.n_pairs = static_cast<int>(pairs.size());
         A.n_kv = static_cast<int>(a->n_kv_heads);
         A.G = static_cast<int>(G);
