@@ -189,20 +189,22 @@ class Runner:
         else:
             self.kv_bytes = w.kv_read_bytes(self.local)
         self.alg_bytes = self.kv_bytes + w.other_bytes(n)
+        self._plan = self.plan()
 
-    def kernel(self, q=None, k=None, v=None, out=None):
+    def plan(self, q=None, k=None, v=None, out=None):
+        """The step's C call with its arguments built once (jx.StepPlan)."""
         q = self.q if q is None else q
         k = self.k if k is None else k
         v = self.v if v is None else v
         out = self.out if out is None else out
-        w, jx = self.w, self.jx
-        if self.mode == "positions":
-            jx.attn_step_partial(self.cache, w.layers, q, k, v, self.partials, self.pos,
-                                 w.n_heads, w.n_kv_heads, scale=w.scale,
-                                 sliding_window=w.window, neox=w.neox)
-        else:
-            jx.attn_step(self.cache, w.layers, q, k, v, out, self.pos, w.n_heads, w.n_kv_heads,
-                         scale=w.scale, sliding_window=w.window, neox=w.neox)
+        w = self.w
+        return self.jx.StepPlan(self.cache, w.layers, q, k, v, out, self.pos, w.n_heads,
+                                w.n_kv_heads, scale=w.scale, sliding_window=w.window,
+                                neox=w.neox,
+                                partials=self.partials if self.mode == "positions" else None)
+
+    def kernel(self, plan=None):
+        (plan or self._plan).run()
 
     def finish(self, out=None):
         """Collective tail of a sharded step (all-gather + log-sum-exp merge)."""
@@ -254,17 +256,21 @@ def run_ours(args, rank, world, local_rank):
 
     sampler = ClockSampler(local_rank)
     sampler.start()
-    # untimed clock probe: leave idle clocks before warm-up
-    t_end = time.time() + args.clock_probe_s
+    # untimed clock probe so clocks leave idle before warm-up.  Every rank runs
+    # the same number of steps (a sharded step holds a collective): time five
+    # steps, size the probe from the slowest rank, then run it.
     n_probe = 0
-    while time.time() < t_end:
-        for _ in range(20):
+    if args.clock_probe_s > 0:
+        t0 = time.time()
+        for _ in range(5):
             r.step()
         torch.cuda.synchronize()
-        n_probe += 20
-    # every rank must take the same collective steps: agree on the probe count
-    if world > 1:
-        n_probe = int(max_over_ranks(n_probe))
+        per_step = max_over_ranks((time.time() - t0) / 5)
+        n_probe = int(min(100000, max(0.0, args.clock_probe_s / max(per_step, 1e-6))))
+        for _ in range(n_probe):
+            r.step()
+        torch.cuda.synchronize()
+        n_probe += 5
     for _ in range(args.warmup):
         r.step()
     torch.cuda.synchronize()
@@ -306,12 +312,13 @@ def run_ours(args, rank, world, local_rank):
         oh = torch.empty(r.out.shape, pin_memory=True)
         qh.copy_(r.q.cpu()); kh.copy_(r.k.cpu()); vh.copy_(r.v.cpu())
         qd, kd, vd, od = (torch.empty_like(x) for x in (r.q, r.k, r.v, r.out))
+        e2e_plan = r.plan(qd, kd, vd, od)
 
         def e2e_step():
             qd.copy_(qh, non_blocking=True)
             kd.copy_(kh, non_blocking=True)
             vd.copy_(vh, non_blocking=True)
-            r.kernel(qd, kd, vd, od)
+            r.kernel(e2e_plan)
             r.finish(od)
             oh.copy_(od, non_blocking=True)
 
@@ -494,6 +501,7 @@ def main():
     import torch
     import torch.distributed as dist
     if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),

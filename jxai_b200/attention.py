@@ -301,6 +301,41 @@ def attn_step_partial(cache: KVCache, layers: Sequence[Layer], q, k, v, partials
                                          _stream_ptr(stream)))
 
 
+class StepPlan:
+    """One attn_step (or attn_step_partial) call with its C arguments built once.
+
+    For callers that repeat the same step on the same buffers (a decode loop
+    whose inputs are rewritten in place, or a benchmark): run() costs one
+    foreign call.  The library additionally recognises an identical call and
+    relaunches the launches it built for it.
+    """
+
+    def __init__(self, cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos: Sequence[int],
+                 n_heads: int, n_kv_heads: int, scale: Optional[float] = None,
+                 softcap: float = 0.0, sliding_window: int = 0, yarn_scale: float = 1.0,
+                 neox: bool = True, seq_ids: Optional[Sequence[int]] = None, partials=None):
+        self.cache = cache
+        self.arr, self._keep = _layer_array(layers)
+        self.args, self._keep2 = _step_args(cache, layers, q, k, v, out if partials is None else None,
+                                            pos, n_heads, n_kv_heads, scale, softcap,
+                                            sliding_window, yarn_scale, neox, seq_ids, 0)
+        self._tensors = (q, k, v, out, partials)
+        self.n_layers = len(layers)
+        if partials is None:
+            self._call = cache.lib.jx_attn_step
+            self._head = (cache.handle, self.arr, self.n_layers, C.byref(self.args))
+        else:
+            hd = layers[0].head_dim
+            pp = _dev_ptr(partials, "partials", len(pos) * len(layers) * n_heads * (hd + 2))
+            self._call = cache.lib.jx_attn_step_partial
+            self._head = (cache.handle, self.arr, self.n_layers, C.byref(self.args), pp)
+
+    def run(self, stream=None) -> None:
+        rc = self._call(*self._head, _stream_ptr(stream))
+        if rc:
+            check(rc)
+
+
 def lse_merge(gathered, n_shards: int, n_groups: int, n_heads: int, head_dim: int, out,
               out_stride: Optional[int] = None, stream=None) -> None:
     """Merge n_shards back-to-back partial buffers into out [n_groups, out_stride]."""

@@ -574,7 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!whole) {
             // Last CTA to finish this segment merges every piece (no waiting).
-            __threadfence();
+            // Release: every writer reaches the barrier, then one thread fences
+            // and counts the piece in (the pattern of a grid-wide barrier).
             named_bar_sync(1, kConsumerThreads);
             const long long c_first = owner_cta(it.seg_start, a.total, P);
             const long long c_last = owner_cta(it.seg_start + pr.len - 1, a.total, P);
@@ -583,29 +584,99 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          61, seg, c_first, c_last)) {
                 misc[0] = 0;
             } else if (ctid == 0) {
-                const int prev = atomicAdd(a.counters + seg, 1);
+                const int prev = atomic_add_acq_rel_gpu(a.counters + seg, 1);
                 const bool last = prev == static_cast<int>(c_last - c_first);
+                if (last) a.counters[seg] = 0;  // every piece has arrived: ready for the next step
                 misc[0] = last ? 1 : 0;
-                if (last) a.counters[seg] = 0;
             }
             named_bar_sync(1, kConsumerThreads);
             if (misc[0]) {
-                __threadfence();
                 // (slots c_first+seg .. c_last+seg were bounds-checked above)
-                for (int idx = ctid; idx < a.G * HD; idx += kConsumerThreads) {
-                    const int g = idx / HD, d = idx % HD;
-                    float M = -INFINITY;
-                    for (long long cc = c_first; cc <= c_last; ++cc)
-                        M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GP + g) * (HD + 2) + HD));
-                    float Lsum = 0.0f, O = 0.0f;
-                    for (long long cc = c_first; cc <= c_last; ++cc) {
-                        const float* src = a.scratch + ((cc + seg) * GP + g) * (HD + 2);
-                        const float mw = __ldcg(src + HD);
-                        const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
-                        Lsum += __ldcg(src + HD + 1) * f;
-                        O += __ldcg(src + d) * f;
+                const int np = static_cast<int>(c_last - c_first + 1);
+                const int Gn = a.G;
+                float* ms = o_s;              // [np][G] piece maxima, then scale factors
+                float* ls = o_s + np * Gn;    // [np][G] piece sums
+                float* tot = ls + np * Gn;    // [G] merged max, [G] merged sum
+                const float* base_p = a.scratch + (c_first + seg) * GP * (HD + 2);
+                if ((2 * np + 2) * Gn <= kConsumerWarps * GP * HD) {
+                    // one parallel pass over every piece's (m, l) ...
+                    for (int idx = ctid; idx < np * Gn; idx += kConsumerThreads) {
+                        const int q = idx / Gn, g = idx % Gn;
+                        const float* src = base_p + (static_cast<long long>(q) * GP + g) * (HD + 2);
+                        ms[idx] = __ldcg(src + HD);
+                        ls[idx] = __ldcg(src + HD + 1);
                     }
-                    emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
+                    named_bar_sync(1, kConsumerThreads);
+                    // ... merged max, scale factors and sum per head ...
+                    for (int g = ctid; g < Gn; g += kConsumerThreads) {
+                        float M = -INFINITY;
+                        for (int q = 0; q < np; ++q) M = fmaxf(M, ms[q * Gn + g]);
+                        float Lsum = 0.0f;
+                        for (int q = 0; q < np; ++q) {
+                            const float mw = ms[q * Gn + g];
+                            const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
+                            ms[q * Gn + g] = f;
+                            Lsum += ls[q * Gn + g] * f;
+                        }
+                        tot[g] = M;
+                        tot[Gn + g] = Lsum;
+                    }
+                    named_bar_sync(1, kConsumerThreads);
+                    // ... then o: every load of a chunk of pieces is issued before any
+                    // is used (one round trip per chunk)
+                    constexpr int E = (GP * HD + kConsumerThreads - 1) / kConsumerThreads;
+                    constexpr int QC = (32 / E) < 1 ? 1 : ((32 / E) > 8 ? 8 : (32 / E));
+                    const long long step = static_cast<long long>(GP) * (HD + 2);
+                    float O[E];
+#pragma unroll
+                    for (int e = 0; e < E; ++e) O[e] = 0.0f;
+                    for (int q0 = 0; q0 < np; q0 += QC) {
+                        float vals[E][QC];
+#pragma unroll
+                        for (int e = 0; e < E; ++e) {
+                            const int idx = ctid + e * kConsumerThreads;
+                            const int g = idx / HD, d = idx % HD;
+                            const float* src = base_p + static_cast<long long>(g) * (HD + 2) + d;
+#pragma unroll
+                            for (int qq = 0; qq < QC; ++qq)
+                                vals[e][qq] = (idx < Gn * HD && q0 + qq < np)
+                                                  ? __ldcg(src + (q0 + qq) * step) : 0.0f;
+                        }
+#pragma unroll
+                        for (int e = 0; e < E; ++e) {
+                            const int idx = ctid + e * kConsumerThreads;
+                            const int g = idx / HD;
+#pragma unroll
+                            for (int qq = 0; qq < QC; ++qq)
+                                if (idx < Gn * HD && q0 + qq < np)
+                                    O[e] += vals[e][qq] * ms[(q0 + qq) * Gn + g];
+                        }
+                    }
+#pragma unroll
+                    for (int e = 0; e < E; ++e) {
+                        const int idx = ctid + e * kConsumerThreads;
+                        if (idx < Gn * HD) {
+                            const int g = idx / HD, d = idx % HD;
+                            emit_final<HD>(a, pr, kvh * Gn + g, d, tot[g], tot[Gn + g], O[e]);
+                        }
+                    }
+                } else {
+                    // more pieces than the staging area holds: merge directly
+                    for (int idx = ctid; idx < Gn * HD; idx += kConsumerThreads) {
+                        const int g = idx / HD, d = idx % HD;
+                        float M = -INFINITY;
+                        for (long long cc = c_first; cc <= c_last; ++cc)
+                            M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GP + g) * (HD + 2) + HD));
+                        float Lsum = 0.0f, O = 0.0f;
+                        for (long long cc = c_first; cc <= c_last; ++cc) {
+                            const float* src = a.scratch + ((cc + seg) * GP + g) * (HD + 2);
+                            const float mw = __ldcg(src + HD);
+                            const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
+                            Lsum += __ldcg(src + HD + 1) * f;
+                            O += __ldcg(src + d) * f;
+                        }
+                        emit_final<HD>(a, pr, kvh * Gn + g, d, M, Lsum, O);
+                    }
                 }
             }
         }

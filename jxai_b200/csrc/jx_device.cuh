@@ -157,6 +157,15 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Atomic add with acquire-release semantics at GPU scope.  Issued by one
+// thread after a CTA barrier, it publishes every write the CTA made before the
+// barrier and observes every write published by earlier arrivals.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 // Named barrier over `count` threads (count a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -260,6 +260,13 @@ struct jx_kv {
     int last_launches = 0;
     // launch shape per (head_dim, group, stages override): {stages, ctas per SM}
     std::map<std::tuple<int, int, int, int>, std::pair<int, int>> shapes;
+    // Replay of the last step: a call identical to the previous one (same
+    // arguments, positions, layers, buffers, stream, options) relaunches the
+    // launches built for it, as long as no plan buffer or scratch changed since.
+    uint64_t generation = 0;  // bumped whenever a plan buffer or the scratch changes
+    uint64_t replay_generation = ~0ull;
+    std::vector<unsigned char> replay_key;
+    std::vector<DecodeLaunch> replay;
 };
 
 namespace {
@@ -320,6 +327,7 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
         s.h_cap = cap;
     }
     std::memcpy(s.h_buf, bytes.data(), bytes.size());
+    ++kv->generation;
     JX_CUDA(cudaMemcpyAsync(s.d_buf, s.h_buf, bytes.size(), cudaMemcpyHostToDevice, stream));
     JX_CUDA(cudaEventRecord(s.ev, stream));
     s.ev_pending = true;
@@ -328,6 +336,7 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
 }
 
 int ensure_scratch(jx_kv* kv, size_t floats, size_t counters) {
+    if (kv->scratch_floats < floats || kv->counters_n < counters) ++kv->generation;
     if (kv->scratch_floats < floats) {
         if (kv->d_scratch) JX_CUDA(cudaFree(kv->d_scratch));
         kv->d_scratch = nullptr;
@@ -363,11 +372,58 @@ int gp_of(uint32_t g) {
     return 0;
 }
 
+template <typename T>
+void put(std::vector<unsigned char>& k, const T& v) {
+    const unsigned char* p = reinterpret_cast<const unsigned char*>(&v);
+    k.insert(k.end(), p, p + sizeof(T));
+}
+
+// Everything a step's launches depend on, field by field (no padding bytes).
+std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers,
+                                    uint32_t n_layers, const jx_step_args* a,
+                                    const float* partials, cudaStream_t stream) {
+    std::vector<unsigned char> k;
+    k.reserve(128 + 8 * a->n_seqs + 40 * n_layers);
+    put(k, a->n_heads); put(k, a->n_kv_heads); put(k, a->n_seqs);
+    put(k, a->q); put(k, a->k); put(k, a->v); put(k, a->out);
+    put(k, a->q_stride); put(k, a->kv_stride); put(k, a->scale); put(k, a->softcap);
+    put(k, a->sliding_window); put(k, a->yarn_scale); put(k, a->rope_neox);
+    put(k, partials); put(k, stream);
+    put(k, kv->opt_stages); put(k, kv->opt_ctas_per_sm); put(k, kv->opt_grid);
+    for (uint32_t s = 0; s < a->n_seqs; ++s) {
+        put(k, a->pos[s]);
+        put(k, a->seq_ids ? a->seq_ids[s] : -1);
+    }
+    for (uint32_t l = 0; l < n_layers; ++l) {
+        const jx_layer_desc& L = layers[l];
+        put(k, L.head_dim); put(k, L.rope_dim); put(k, L.rope_freq_base);
+        put(k, L.kv_source_layer); put(k, L.is_swa); put(k, L.shares_kv);
+        put(k, L.rope_freqs ? hash_floats(L.rope_freqs, std::min(L.head_dim, L.rope_dim) / 2)
+                            : uint64_t(0));
+    }
+    return k;
+}
+
 int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
               float* partials, cudaStream_t stream) {
     if (!kv || !layers || !a) return fail(JX_ERR_INVALID, "null handle, layers or args");
     if (n_layers == 0 || a->n_seqs == 0) return fail(JX_ERR_INVALID, "empty step");
     if (!a->pos || !a->q || !a->k || !a->v) return fail(JX_ERR_INVALID, "null pos/q/k/v");
+    std::vector<unsigned char> key = call_key(kv, layers, n_layers, a, partials, stream);
+    if (kv->replay_generation == kv->generation && key == kv->replay_key) {
+        DeviceGuard guard(kv->d.device);
+        if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
+        for (const DecodeLaunch& Lc : kv->replay) {
+            const cudaError_t e = decode_launch(Lc);
+            if (e != cudaSuccess)
+                return fail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+        }
+        kv->last_launches = static_cast<int>(kv->replay.size());
+        return JX_OK;
+    }
+    kv->replay_generation = ~0ull;
+    kv->replay.clear();
+    std::vector<DecodeLaunch> launched;
     const bool partial = partials != nullptr;
     if (!partial && !a->out) return fail(JX_ERR_INVALID, "null out");
     if (a->n_kv_heads == 0 || a->n_heads == 0 || a->n_heads % a->n_kv_heads != 0)
@@ -632,8 +688,12 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         if (e != cudaSuccess)
             return fail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
         ++launches;
+        launched.push_back(Lc);
     }
     kv->last_launches = launches;
+    kv->replay_key = std::move(key);
+    kv->replay = std::move(launched);
+    kv->replay_generation = kv->generation;
     return JX_OK;
 }
 

@@ -203,3 +203,43 @@ def test_wide_heads_long_pieces(hd, stages):
                       1 / math.sqrt(hd), neox=True)
     assert np.abs(out.cpu().numpy() - ref).max() <= TOL
     cache.close()
+
+
+def test_repeated_and_alternating_calls():
+    # an identical call relaunches the launches built for it; a call with other
+    # positions rebuilds the plan; going back must not reuse stale launches
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(23)
+    H, HK, hd, L = 8, 2, 64, 2
+    cap, rs = 400, HK * hd
+    kc = rng.standard_normal((2, L, cap, rs)).astype(np.float32)
+    vc = rng.standard_normal((2, L, cap, rs)).astype(np.float32)
+    q = rng.standard_normal((2, L, H * hd)).astype(np.float32)
+    k = rng.standard_normal((2, L, HK * hd)).astype(np.float32)
+    v = rng.standard_normal((2, L, HK * hd)).astype(np.float32)
+    layers = [jx.Layer(hd, hd, 1e6, l) for l in range(L)]
+    cache = jx.KVCache(2, L, cap, rs, "f32")
+    for s in range(2):
+        for l in range(L):
+            cache.write_rows(s, l, 0, 0, kc[s, l])
+            cache.write_rows(s, l, 1, 0, vc[s, l])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    ko, vo = kc.copy(), vc.copy()
+    refs = {}
+    # b appends rows (350, 399), outside a's attended rows (<= 300, <= 120); b attends
+    # over a's appended rows, so its reference is taken after a's step
+    for pos in ([300, 120], [350, 399]):
+        refs[tuple(pos)] = oracle_step(ko, vo, F32, pos, layers, q, k, v, H, HK, hd,
+                                       1 / math.sqrt(hd))
+    out = torch.zeros_like(qd)
+    plan_a = jx.StepPlan(cache, layers, qd, kd, vd, out, [300, 120], H, HK)
+    plan_b = jx.StepPlan(cache, layers, qd, kd, vd, out, [350, 399], H, HK)
+    for seq in ("a", "a", "b", "a", "b", "b", "a"):
+        out.fill_(float("nan"))
+        (plan_a if seq == "a" else plan_b).run()
+        torch.cuda.synchronize()
+        ref = refs[(300, 120)] if seq == "a" else refs[(350, 399)]
+        assert np.abs(out.cpu().numpy() - ref).max() <= TOL, seq
+    assert cache.check_device_error() == 0
+    cache.close()
