@@ -255,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int stage = 0;         // tile % NS
         uint32_t phase = 0;    // (tile / NS) & 1
         int n_issued = 0;  // tiles [0, n_issued) had their loads issued
+        int piece = 0;
         while (it.next()) {
             const PairRow& pr = it.pr;
             const int ntiles = (it.n + kTileRows - 1) / kTileRows;
@@ -264,11 +265,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    pr.row0 + pr.len <= a.capacity,
                             30, it.kvh, pr.cache_layer, pr.row0 + pr.len))
                 break;
+            // Tile holding the segment's newest row, when this piece holds it; the
+            // row is stored (and fenced) before that tile is loaded.  In the CTA's
+            // first piece -- the kernel's ramp, ring empty -- that is just before
+            // the tile; later pieces find the ring full of the previous piece, so
+            // their append goes first and its latency hides behind those tiles.
             int t_app = -1;
             if (pr.append_row >= 0) {
                 const int al = pr.append_row - pr.row0;
                 if (al >= it.r && al < it.r + it.n) t_app = (al - it.r) / kTileRows;
             }
+            if (piece > 0 && t_app >= 0) t_app = 0;
+            ++piece;
             for (int t = 0; t < ntiles; ++t, ++tile) {
                 if (t == t_app) {
                     append_slice<HD, DT>(a, pr, it.kvh, lane);
