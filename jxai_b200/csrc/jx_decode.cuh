@@ -16,12 +16,18 @@
 //    multiple of C, so every use of a given stage is consumed by the same warp,
 //    in order.  (A stage whose successive uses went to different warps could be
 //    waited on two phases ahead, which mbarrier parity cannot tell apart.)
-//  * Math on CUDA cores (the step is HBM-bound: ~2 flop per KV byte at group 4).
-//    QK: lane = cache row, dot product over head_dim in ascending order with
-//    fused multiply-adds (the reference's `dot += q[d]*k[d]` order), q of the
-//    whole query group broadcast from shared memory.  Online softmax per tile
-//    with warp-shuffle max; PV: lane = head dimensions, p broadcast from
-//    shared memory.
+//  * fp32 caches: math on CUDA cores (~1 flop per KV byte at group 4, well
+//    under the FMA rate at HBM speed).  QK: lane = cache row, dot product over
+//    head_dim in ascending order with fused multiply-adds (the reference's
+//    `dot += q[d]*k[d]` order), q of the whole query group broadcast from
+//    shared memory.  Online softmax per tile with warp-shuffle max; PV: lane =
+//    head dimensions, p broadcast from shared memory.
+//  * bf16 / fp16 caches: twice the flops per byte plus a conversion per
+//    element made the CUDA-core form FMA-issue-bound (~60% of HBM), so QK and
+//    PV run on the tensor cores (MmaWarp: warp-level m16n8k16, q and p split
+//    into two 16-bit parts for fp32-level accuracy).  Two kv heads share a
+//    tile row where head rows are under 256 bytes (kv_pack), each handled by
+//    its own consumer warp.
 //  * Merge.  At the end of a piece the four warps' (m, l, o) are merged through
 //    shared memory.  A piece that is a whole segment writes the normalised
 //    output directly; otherwise it writes a partial to scratch and the last
@@ -63,14 +69,16 @@ struct Geo {
     static_assert(ROWB % 64 == 0, "row bytes must be a multiple of 64");
 };
 
-// Shared-memory carve-up, identical on host and device.
-template <int HD, int GP, int DT>
+// Shared-memory carve-up, identical on host and device.  KP kv heads share a
+// tile row (16-bit caches), so a segment has GP*KP query heads.
+template <int HD, int GP, int DT, int KP = 1>
 struct SmemLayout {
-    using G = Geo<HD, DT>;
-    static constexpr int q_bytes = GP * HD * 4;
-    static constexpr int p_bytes = kConsumerWarps * kTileRows * GP * 4;
-    static constexpr int o_bytes = kConsumerWarps * GP * HD * 4;
-    static constexpr int ml_bytes = kConsumerWarps * GP * 2 * 4;
+    using G = Geo<HD * KP, DT>;
+    static constexpr int GS = GP * KP;
+    static constexpr int q_bytes = GS * HD * 4;
+    static constexpr int p_bytes = DT == DT_F32 ? kConsumerWarps * kTileRows * GS * 4 : 0;
+    static constexpr int o_bytes = kConsumerWarps * GS * HD * 4;
+    static constexpr int ml_bytes = kConsumerWarps * GS * 2 * 4;
     static constexpr int misc_bytes = 16;
     static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
     static __host__ __device__ constexpr int bars_offset(int ns) {
@@ -163,14 +171,14 @@ __device__ __forceinline__ long long owner_cta(long long x, long long total, lon
 // (transformer.cpp:2506-2520), one warp.
 template <int HD, int DT>
 __device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow& pr, int kvh,
-                                             int lane) {
+                                             int kp, int lane) {
     const float* kin = a.k_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
     const float* vin = a.v_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
     const long long dst = static_cast<long long>(pr.seq) * a.seq_stride +
                           static_cast<long long>(pr.cache_layer) * a.layer_stride +
                           static_cast<long long>(pr.append_row) * a.row_stride + kvh * HD;
     const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
-    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && kvh < a.n_kv, 10, pr.io, kvh, 0)) return;
+    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && kvh < a.n_kv * kp, 10, pr.io, kvh, 0)) return;
     if (!JX_CHECKED(a, dst >= 0 && dst + HD <= a.cache_elems, 11, dst, pr.append_row, pr.seq)) return;
     if (!JX_CHECKED(a, pr.rope_row >= 0 && pr.rope_row < a.n_rope_rows, 12, pr.rope_row, 0, 0)) return;
 #pragma unroll 2
@@ -200,37 +208,304 @@ __device__ __forceinline__ void emit_final(const DecodeArgs& a, const PairRow& p
     }
 }
 
-template <int HD, int GP, int DT>
+// ---------------------------------------------------------------- 16-bit caches: warp MMA
+// One consumer warp's attention state for bf16 / fp16 caches, on the tensor
+// cores (mma.sync m16n8k16, fp32 accumulation).  Per 32-row tile:
+//   S^T[row][col] = K[row][:] . Qc[col][:]     rows as M (two blocks of 16)
+//   O^T[d][col]  += V^T[d][row] . Pc[row][col]  head dims as M (HD/16 blocks)
+// The 8 columns of an n8 block are (part, head) pairs, col = part*GP + head:
+// q and p are fp32, so each is split into two 16-bit parts, hi = rn(x) and
+// lo = rn(x - hi), and the parts' columns are summed back in fp32.  Cache
+// values are exact in the MMA's operand type, so the products carry q and p
+// to ~2^-17 relative (bf16) or ~2^-22 (fp16), inside the fp32-path tolerance.
+// fp16 q is first scaled by a power of two so the group's largest |q| sits in
+// [2^14, 2^15) (no overflow, no lost low bits); the scale is undone on S
+// exactly.  Lane L holds, after the column sums, S and O for the rows / dims
+// of its C fragment and heads (2(L%4) + j) % GP, j = 0, 1 ("slots").
+template <int HD, int GP, int DT, int KP>
+struct MmaWarp {
+    static constexpr int RW = HD * KP;            // tile row: KP kv heads side by side
+    using G = Geo<RW, DT>;
+    static constexpr int NBC = (2 * GP + 7) / 8;  // n8 blocks of (part, head) columns
+    static constexpr int KS = HD / 16;            // k16 steps of QK = m16 blocks of PV
+    static_assert(DT != DT_F32, "fp32 caches use the CUDA-core consumer");
+    static_assert(HD % 16 == 0, "head_dim must be a multiple of 16");
+
+    int kp;                   // the kv head of the tile row this warp attends with
+    uint32_t qf[KS][NBC][2];  // Q^T B fragments
+    float o[KS][NBC][4];      // O^T accumulators
+    float m[2], l[2];         // running max / lane-partial sum per slot
+    float s_unscale;          // 2^-shift of the fp16 q scaling (1 for bf16)
+
+    // Sum of a value over the columns that hold the same head (see above).
+    __device__ __forceinline__ static float col_sum(const float (&x)[NBC][4], int r) {
+        float v = x[0][r];
+        if constexpr (NBC == 2) v += x[1][r];
+        if constexpr (GP == 1) v += x[0][r ^ 1];
+        if constexpr (GP <= 2) v += __shfl_xor_sync(0xffffffffu, v, 1);
+        if constexpr (GP <= 4) v += __shfl_xor_sync(0xffffffffu, v, 2);
+        return v;
+    }
+
+    // This lane's 16-bit pair for column block nb from the hi / lo pairs.
+    __device__ __forceinline__ static uint32_t pick(uint32_t hi, uint32_t lo, int nb, int t) {
+        if constexpr (GP == 8) return nb == 0 ? hi : lo;
+        else if constexpr (GP == 4) return t < 2 ? hi : lo;
+        else if constexpr (GP == 2) return t == 0 ? hi : (t == 1 ? lo : 0u);
+        else return t == 0 ? ((hi & 0xFFFFu) | (lo << 16)) : 0u;  // cols 0, 1 = hi, lo
+    }
+
+    // q_s: rotated q of the segment's KP*GP heads, [head][HD]; this warp takes
+    // kv head `kp_` of the tile row and its GP query heads.
+    __device__ __forceinline__ void begin_piece(const float* q_s, int lane, int kp_) {
+        kp = kp_;
+        const int g = lane >> 2, t = lane & 3;
+        float x[KS][NBC][4];
+        float mx = 0.0f;
+#pragma unroll
+        for (int nb = 0; nb < NBC; ++nb) {
+            const int col = nb * 8 + g;
+            const int part = col / GP, h = col % GP;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const float* src = q_s + (kp * GP + h) * HD + ks * 16 + 2 * t;
+                const bool use = part < 2;
+                x[ks][nb][0] = use ? src[0] : 0.0f;
+                x[ks][nb][1] = use ? src[1] : 0.0f;
+                x[ks][nb][2] = use ? src[8] : 0.0f;
+                x[ks][nb][3] = use ? src[9] : 0.0f;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(x[ks][nb][e]));
+            }
+        }
+        float up = 1.0f;
+        s_unscale = 1.0f;
+        if constexpr (DT == DT_F16T) {
+            const float gm = warp_max(mx);
+            const int e = static_cast<int>((__float_as_uint(gm) >> 23) & 0xFFu) - 127;
+            const int sh = min(60, max(-60, 14 - e));
+            up = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
+            s_unscale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+        }
+#pragma unroll
+        for (int nb = 0; nb < NBC; ++nb) {
+            const int part = (nb * 8 + g) / GP;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                uint32_t h01, l01, h23, l23;
+                split_pair<DT>(x[ks][nb][0] * up, x[ks][nb][1] * up, h01, l01);
+                split_pair<DT>(x[ks][nb][2] * up, x[ks][nb][3] * up, h23, l23);
+                qf[ks][nb][0] = part == 0 ? h01 : (part == 1 ? l01 : 0u);
+                qf[ks][nb][1] = part == 0 ? h23 : (part == 1 ? l23 : 0u);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            m[j] = -INFINITY;
+            l[j] = 0.0f;
+        }
+#pragma unroll
+        for (int mh = 0; mh < KS; ++mh)
+#pragma unroll
+            for (int nb = 0; nb < NBC; ++nb)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) o[mh][nb][r] = 0.0f;
+    }
+
+    // One tile of kTileRows rows; rows [nvalid, kTileRows) are not attended.
+    __device__ __forceinline__ void tile(uint32_t Kt, unsigned char* Vt_ptr, uint32_t Vt,
+                                         int nvalid, int lane, float scale, float softcap,
+                                         float inv_cap) {
+        const int g = lane >> 2, t = lane & 3;
+        const int i8 = lane >> 3, r8 = lane & 7;
+        const int cb = kp * HD * 2;  // this kv head's first byte in a tile row
+        if (nvalid < kTileRows) {
+            // p is 0 there, but 0 * (Inf or NaN) is not: clear this kv head's
+            // unattended V rows
+            constexpr int CH = HD * 2 / 16;
+            for (int idx = lane; idx < (kTileRows - nvalid) * CH; idx += 32) {
+                const int row = nvalid + idx / CH;
+                *reinterpret_cast<uint4*>(Vt_ptr + tile_off<RW, DT>(row, cb + (idx % CH) * 16)) =
+                    make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_shared();  // before the stage's next TMA write
+            __syncwarp();
+        }
+        // ---- S^T = K Qc^T
+        float acc[2][NBC][4];
+#pragma unroll
+        for (int mb = 0; mb < 2; ++mb)
+#pragma unroll
+            for (int nb = 0; nb < NBC; ++nb)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[mb][nb][r] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+            for (int mb = 0; mb < 2; ++mb) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4<false>(Kt + tile_off<RW, DT>(mb * 16 + (i8 & 1) * 8 + r8,
+                                                     cb + ks * 32 + (i8 >> 1) * 16),
+                               a0, a1, a2, a3);
+#pragma unroll
+                for (int nb = 0; nb < NBC; ++nb)
+                    mma_16816<DT>(acc[mb][nb], a0, a1, a2, a3, qf[ks][nb][0], qf[ks][nb][1]);
+            }
+        }
+        // ---- scores, online softmax (rows mb*16 + (r>>1)*8 + g, slot r&1)
+        float s[2][4];
+#pragma unroll
+        for (int mb = 0; mb < 2; ++mb)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                float sc = __fmul_rn(col_sum(acc[mb], r) * s_unscale, scale);
+                if (softcap > 0.0f) sc = __fmul_rn(softcap, tanhf(__fmul_rn(sc, inv_cap)));
+                s[mb][r] = mb * 16 + (r >> 1) * 8 + g < nvalid ? sc : -INFINITY;
+            }
+        float alpha[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float mt = fmaxf(fmaxf(s[0][j], s[0][j + 2]), fmaxf(s[1][j], s[1][j + 2]));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+            const float mn = fmaxf(m[j], mt);
+            alpha[j] = m[j] == -INFINITY ? 0.0f : ex2_approx((m[j] - mn) * kLog2e);
+            m[j] = mn;
+        }
+        float p[2][4];
+        float ls[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int mb = 0; mb < 2; ++mb)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                p[mb][r] = ex2_approx((s[mb][r] - m[r & 1]) * kLog2e);
+                ls[r & 1] += p[mb][r];
+            }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) l[j] = l[j] * alpha[j] + ls[j];
+#pragma unroll
+        for (int mh = 0; mh < KS; ++mh)
+#pragma unroll
+            for (int nb = 0; nb < NBC; ++nb)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) o[mh][nb][r] *= alpha[r & 1];
+        // ---- P as B fragments: C layout of (rows, columns) -> transposed
+        uint32_t bp[2][NBC][2];
+#pragma unroll
+        for (int mb = 0; mb < 2; ++mb)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                uint32_t hi, lo;
+                split_pair<DT>(p[mb][2 * hf], p[mb][2 * hf + 1], hi, lo);
+#pragma unroll
+                for (int nb = 0; nb < NBC; ++nb) bp[mb][nb][hf] = movmatrix_trans(pick(hi, lo, nb, t));
+            }
+        // ---- O^T += V^T Pc
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+            if (kb == 1 && nvalid <= 16) break;
+#pragma unroll
+            for (int mh = 0; mh < KS; ++mh) {
+                uint32_t a0, a1, a2, a3;
+                ldsm_x4<true>(Vt + tile_off<RW, DT>(kb * 16 + (i8 >> 1) * 8 + r8,
+                                                    cb + mh * 32 + (i8 & 1) * 16),
+                              a0, a1, a2, a3);
+#pragma unroll
+                for (int nb = 0; nb < NBC; ++nb)
+                    mma_16816<DT>(o[mh][nb], a0, a1, a2, a3, bp[kb][nb][0], bp[kb][nb][1]);
+            }
+        }
+    }
+
+    // Writes this warp's (m, l) and unnormalised o per head into the merge
+    // staging area ([warp][KP*GP heads]), in the layout of the CUDA-core
+    // consumer; the heads of the row's other kv heads get the empty state.
+    __device__ __forceinline__ void finish(float* o_s, float* ml_s, int warp, int lane) {
+        constexpr int GS = KP * GP;
+        const int g = lane >> 2, t = lane & 3;
+        float lt[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float v = l[j];
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            lt[j] = v;
+        }
+        // lanes holding a head's first copy write it
+        const bool w0 = GP == 8 || (GP == 4 && t < 2) || (GP <= 2 && t == 0);
+        const bool w1 = w0 && GP != 1;
+#pragma unroll
+        for (int mh = 0; mh < KS; ++mh)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float v = col_sum(o[mh], r);
+                const int j = r & 1;
+                if (j == 0 ? w0 : w1) {
+                    const int h = kp * GP + (2 * t + j) % GP;
+                    o_s[(warp * GS + h) * HD + mh * 16 + (r >> 1) * 8 + g] = v;
+                }
+            }
+        if (g == 0) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (j == 0 ? w0 : w1) {
+                    const int h = kp * GP + (2 * t + j) % GP;
+                    ml_s[(warp * GS + h) * 2] = m[j];
+                    ml_s[(warp * GS + h) * 2 + 1] = lt[j];
+                }
+        }
+        if constexpr (KP > 1) {
+            for (int idx = lane; idx < GS * HD; idx += 32) {
+                const int h = idx / HD;
+                if (h / GP == kp) continue;
+                o_s[(warp * GS + h) * HD + idx % HD] = 0.0f;
+                if (idx % HD == 0) {
+                    ml_s[(warp * GS + h) * 2] = -INFINITY;
+                    ml_s[(warp * GS + h) * 2 + 1] = 0.0f;
+                }
+            }
+        }
+    }
+};
+
+template <int HD, int GP, int DT, int KP>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeArgs a) {
-    using G = Geo<HD, DT>;
-    using L = SmemLayout<HD, GP, DT>;
+    constexpr int RW = HD * KP;  // tile row width (elements): KP kv heads side by side
+    constexpr int GS = GP * KP;  // padded query heads of a segment
+    static_assert(KP == 1 || DT != DT_F32, "kv-head packing is for 16-bit caches");
+    constexpr bool kMma = DT != DT_F32;  // 16-bit caches: tensor-core consumer
+    constexpr int kSplit = KP;           // consumer warps per tile
+    using G = Geo<RW, DT>;
+    using L = SmemLayout<HD, GP, DT, KP>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw_u32 = smem_u32(smem_raw);
     const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
     unsigned char* base = smem_raw + (base_u32 - raw_u32);
     const int NS = a.n_stages;
     float* q_s = reinterpret_cast<float*>(base + L::stages_bytes(NS));
-    float* p_s = q_s + GP * HD;
-    float* o_s = p_s + kConsumerWarps * kTileRows * GP;
-    float* ml_s = o_s + kConsumerWarps * GP * HD;
-    int* misc = reinterpret_cast<int*>(ml_s + kConsumerWarps * GP * 2);
+    float* p_s = q_s + L::q_bytes / 4;
+    float* o_s = p_s + L::p_bytes / 4;
+    float* ml_s = o_s + L::o_bytes / 4;
+    int* misc = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);
     const uint32_t bars = base_u32 + L::bars_offset(NS);  // full[s] at bars+8s, empty[s] at bars+8(NS+s)
     volatile int* abort_flag = misc + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) + 16 * NS <= a.smem_bytes &&
-                           a.n_consumers >= 1 && a.n_consumers <= kConsumerWarps &&
-                           NS % a.n_consumers == 0,
+                           a.n_consumers >= kSplit && a.n_consumers <= kConsumerWarps &&
+                           a.n_consumers % kSplit == 0 && NS % (a.n_consumers / kSplit) == 0,
                     1, a.smem_bytes, NS, a.n_consumers))
         return;  // every thread takes this branch together
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(bars + 8 * s, 1);
-            mbar_init(bars + 8 * (NS + s), 1);
+            mbar_init(bars + 8 * (NS + s), kSplit);
         }
         misc[0] = 0;
         misc[1] = 0;
@@ -279,7 +554,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++piece;
             for (int t = 0; t < ntiles; ++t, ++tile) {
                 if (t == t_app) {
-                    append_slice<HD, DT>(a, pr, it.kvh, lane);
+#pragma unroll
+                    for (int kp = 0; kp < KP; ++kp)
+                        append_slice<HD, DT>(a, pr, it.kvh * KP + kp, KP, lane);
                     fence_proxy_async_global();
                     __syncwarp();
                 }
@@ -303,12 +580,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t dv = dk + G::TILEB;
                     const int row = pr.row0 + it.r + t * kTileRows;
                     if (JX_CHECKED(a, stage_ >= 0 && stage_ < NS && row >= 0 && row < a.capacity &&
-                                          (it.kvh + 1) * HD <= a.row_stride,
+                                          (it.kvh + 1) * RW <= a.row_stride,
                                    31, row, stage_, it.kvh)) {
                         mbar_arrive_expect_tx(fb, 2 * G::TILEB);
 #pragma unroll
                         for (int b = 0; b < G::NB; ++b) {
-                            const int c0 = it.kvh * HD + b * G::BOXE;
+                            const int c0 = it.kvh * RW + b * G::BOXE;
                             tma_load_4d(dk + b * kTileRows * G::BOX, &tmK, fb, c0, row,
                                         pr.cache_layer, pr.seq);
                             tma_load_4d(dv + b * kTileRows * G::BOX, &tmV, fb, c0, row,
@@ -350,13 +627,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     it.init(a.pairs, a.n_pairs, a.n_kv, b0, b1, a.cta_pair);
     const int C = a.n_consumers;
     const bool active = warp < C;
+    // 16-bit caches with two kv heads per tile row: each tile goes to a pair of
+    // warps, one per kv head (SPLIT arrivals release a stage)
+    const int streams = C / kSplit;  // tile streams; stream i takes tiles i, i + streams, ...
+    const int stream_id = warp / kSplit;
     int tile_base = 0;          // global index of the current piece's first tile
-    int my_k = warp;            // this warp's next tile (global index)
-    int my_stage = warp;        // my_k % NS
+    int my_k = stream_id;       // this warp's next tile (global index)
+    int my_stage = stream_id;   // my_k % NS
     uint32_t my_phase = 0;      // (my_k / NS) & 1
     const float scale = a.scale;
     const float softcap = a.softcap;
     const float inv_cap = a.inv_softcap;
+    using MW = MmaWarp<HD, GP, (kMma ? DT : DT_BF16), KP>;
+    MW mw;
     while (it.next()) {
         const PairRow& pr = it.pr;
         const int kvh = it.kvh;
@@ -369,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* qin = a.q + static_cast<long long>(pr.io) * a.q_stride +
                                static_cast<long long>(kvh) * a.G * HD;
             const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
-            for (int idx = ctid; idx < GP * HD; idx += kConsumerThreads) {
+            for (int idx = ctid; idx < GS * HD; idx += kConsumerThreads) {
                 const int g = idx / HD, d = idx % HD;
                 q_s[idx] = g < a.G ? rope_elem(qin + g * HD, d, pr.rope_half, cs, a.neox != 0)
                                    : 0.0f;
@@ -377,13 +660,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_bar_sync(1, kConsumerThreads);
 
-        float m[GP], l[GP], o[GP][G::DPL];
+        float m[GS], l[GS], o[GS][G::DPL];
+        if constexpr (kMma) {
+            mw.begin_piece(q_s, lane, warp % kSplit);
+        } else {
 #pragma unroll
-        for (int g = 0; g < GP; ++g) {
-            m[g] = -INFINITY;
-            l[g] = 0.0f;
+            for (int g = 0; g < GS; ++g) {
+                m[g] = -INFINITY;
+                l[g] = 0.0f;
 #pragma unroll
-            for (int k = 0; k < G::DPL; ++k) o[g][k] = 0.0f;
+                for (int k = 0; k < G::DPL; ++k) o[g][k] = 0.0f;
+            }
         }
 
         const int ntiles = (it.n + kTileRows - 1) / kTileRows;
@@ -396,23 +683,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nvalid = min(kTileRows, it.n - t * kTileRows);
             const unsigned char* Kt = base + my_stage * 2 * G::TILEB;
             const unsigned char* Vt = Kt + G::TILEB;
+            if constexpr (kMma) {
+                const uint32_t ku = base_u32 + my_stage * 2 * G::TILEB;
+                mw.tile(ku, base + my_stage * 2 * G::TILEB + G::TILEB, ku + G::TILEB, nvalid,
+                        lane, scale, softcap, inv_cap);
+            } else {
 
             // ---- scores: lane = row
-            float s[GP];
+            float s[GS];
             if (lane < nvalid) {
-                float acc[GP];
+                float acc[GS];
 #pragma unroll
-                for (int g = 0; g < GP; ++g) acc[g] = 0.0f;
+                for (int g = 0; g < GS; ++g) acc[g] = 0.0f;
 #pragma unroll 4
                 for (int j = 0; j < G::CHUNKS; ++j) {
                     const uint4 raw = *reinterpret_cast<const uint4*>(
-                        Kt + tile_off<HD, DT>(lane, j * 16));
+                        Kt + tile_off<RW, DT>(lane, j * 16));
                     float kv[G::EPC];
                     unpack16<DT>(raw, kv);
 #pragma unroll
                     for (int e4 = 0; e4 < G::EPC; e4 += 4) {
 #pragma unroll
-                        for (int g = 0; g < GP; ++g) {
+                        for (int g = 0; g < GS; ++g) {
                             const float4 qv =
                                 *reinterpret_cast<const float4*>(q_s + g * HD + j * G::EPC + e4);
                             acc[g] = __fmaf_rn(qv.x, kv[e4 + 0], acc[g]);
@@ -423,20 +715,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
 #pragma unroll
-                for (int g = 0; g < GP; ++g) {
+                for (int g = 0; g < GS; ++g) {
                     float sc = __fmul_rn(acc[g], scale);
                     if (softcap > 0.0f) sc = __fmul_rn(softcap, tanhf(__fmul_rn(sc, inv_cap)));
                     s[g] = sc;
                 }
             } else {
 #pragma unroll
-                for (int g = 0; g < GP; ++g) s[g] = -INFINITY;
+                for (int g = 0; g < GS; ++g) s[g] = -INFINITY;
             }
 
             // ---- online softmax over this tile
-            float pv[GP];
+            float pv[GS];
 #pragma unroll
-            for (int g = 0; g < GP; ++g) {
+            for (int g = 0; g < GS; ++g) {
                 const float mt = warp_max(s[g]);
                 const float mn = fmaxf(m[g], mt);
                 const float alpha = m[g] == -INFINITY ? 0.0f : ex2_approx((m[g] - mn) * kLog2e);
@@ -447,25 +739,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                 m[g] = mn;
                 pv[g] = p;
             }
-            float* pw = p_s + warp * kTileRows * GP;
-            if constexpr (GP % 4 == 0) {
+            float* pw = p_s + warp * kTileRows * GS;
+            if constexpr (GS % 4 == 0) {
 #pragma unroll
-                for (int g4 = 0; g4 < GP; g4 += 4)
-                    *reinterpret_cast<float4*>(pw + lane * GP + g4) =
+                for (int g4 = 0; g4 < GS; g4 += 4)
+                    *reinterpret_cast<float4*>(pw + lane * GS + g4) =
                         make_float4(pv[g4], pv[g4 + 1], pv[g4 + 2], pv[g4 + 3]);
             } else {
 #pragma unroll
-                for (int g = 0; g < GP; ++g) pw[lane * GP + g] = pv[g];
+                for (int g = 0; g < GS; ++g) pw[lane * GS + g] = pv[g];
             }
             __syncwarp();
 
             // ---- PV: lane = head dims [lane*DPL, lane*DPL + DPL)
             auto pv_row = [&](const int rr) {
-                float pr_[GP];
-                if constexpr (GP % 4 == 0) {
+                float pr_[GS];
+                if constexpr (GS % 4 == 0) {
 #pragma unroll
-                    for (int g4 = 0; g4 < GP; g4 += 4) {
-                        const float4 t4 = *reinterpret_cast<const float4*>(pw + rr * GP + g4);
+                    for (int g4 = 0; g4 < GS; g4 += 4) {
+                        const float4 t4 = *reinterpret_cast<const float4*>(pw + rr * GS + g4);
                         pr_[g4] = t4.x;
                         pr_[g4 + 1] = t4.y;
                         pr_[g4 + 2] = t4.z;
@@ -473,19 +765,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int g = 0; g < GP; ++g) pr_[g] = pw[rr * GP + g];
+                    for (int g = 0; g < GS; ++g) pr_[g] = pw[rr * GS + g];
                 }
                 float vv[G::DPL];
                 if constexpr (G::LANEB >= 16) {
 #pragma unroll
                     for (int q16 = 0; q16 < G::LANEB / 16; ++q16) {
                         const uint4 raw = *reinterpret_cast<const uint4*>(
-                            Vt + tile_off<HD, DT>(rr, lane * G::LANEB + q16 * 16));
+                            Vt + tile_off<RW, DT>(rr, lane * G::LANEB + q16 * 16));
                         unpack16<DT>(raw, vv + q16 * G::EPC);
                     }
                 } else if constexpr (G::LANEB == 8) {
                     const uint2 raw =
-                        *reinterpret_cast<const uint2*>(Vt + tile_off<HD, DT>(rr, lane * 8));
+                        *reinterpret_cast<const uint2*>(Vt + tile_off<RW, DT>(rr, lane * 8));
                     if constexpr (DT == DT_F32) {
                         vv[0] = __uint_as_float(raw.x);
                         vv[1] = __uint_as_float(raw.y);
@@ -498,7 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else if constexpr (G::LANEB == 4) {
                     const uint32_t raw =
-                        *reinterpret_cast<const uint32_t*>(Vt + tile_off<HD, DT>(rr, lane * 4));
+                        *reinterpret_cast<const uint32_t*>(Vt + tile_off<RW, DT>(rr, lane * 4));
                     if constexpr (DT == DT_F32) {
                         vv[0] = __uint_as_float(raw);
                     } else if constexpr (DT == DT_BF16) {
@@ -510,11 +802,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 } else {  // 2 bytes: one 16-bit element
                     const uint32_t raw =
-                        *reinterpret_cast<const uint16_t*>(Vt + tile_off<HD, DT>(rr, lane * 2));
+                        *reinterpret_cast<const uint16_t*>(Vt + tile_off<RW, DT>(rr, lane * 2));
                     vv[0] = DT == DT_BF16 ? bf16_bits_to_f32(raw) : f16_bits_to_f32(raw);
                 }
 #pragma unroll
-                for (int g = 0; g < GP; ++g)
+                for (int g = 0; g < GS; ++g)
 #pragma unroll
                     for (int k = 0; k < G::DPL; ++k) o[g][k] = __fmaf_rn(pr_[g], vv[k], o[g][k]);
             
@@ -526,10 +818,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 2
                 for (int rr = 0; rr < nvalid; ++rr) pv_row(rr);
             }
+            }  // CUDA-core tile
             __syncwarp();
             if (lane == 0) mbar_arrive(bars + 8 * (NS + my_stage));
-            my_k += C;
-            my_stage += C;
+            my_k += streams;
+            my_stage += streams;
             if (my_stage >= NS) {
                 my_stage -= NS;
                 my_phase ^= 1u;
@@ -538,19 +831,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_base = tile_end;
 
         // ---- merge the four warps' states for this piece
+        if constexpr (kMma) {
+            mw.finish(o_s, ml_s, warp, lane);
+        } else {
 #pragma unroll
-        for (int g = 0; g < GP; ++g) l[g] = warp_sum(l[g]);
-        if (lane == 0) {
+            for (int g = 0; g < GS; ++g) l[g] = warp_sum(l[g]);
+            if (lane == 0) {
 #pragma unroll
-            for (int g = 0; g < GP; ++g) {
-                ml_s[(warp * GP + g) * 2] = m[g];
-                ml_s[(warp * GP + g) * 2 + 1] = l[g];
+                for (int g = 0; g < GS; ++g) {
+                    ml_s[(warp * GS + g) * 2] = m[g];
+                    ml_s[(warp * GS + g) * 2 + 1] = l[g];
+                }
             }
+#pragma unroll
+            for (int g = 0; g < GS; ++g)
+#pragma unroll
+                for (int k = 0; k < G::DPL; ++k)
+                    o_s[(warp * GS + g) * HD + lane * G::DPL + k] = o[g][k];
         }
-#pragma unroll
-        for (int g = 0; g < GP; ++g)
-#pragma unroll
-            for (int k = 0; k < G::DPL; ++k) o_s[(warp * GP + g) * HD + lane * G::DPL + k] = o[g][k];
         named_bar_sync(1, kConsumerThreads);
 
         const bool whole = it.r == 0 && it.n == pr.len;
@@ -560,19 +858,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int g = idx / HD, d = idx % HD;
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml_s[(w * GP + g) * 2]);
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, ml_s[(w * GS + g) * 2]);
             float Lsum = 0.0f, O = 0.0f;
 #pragma unroll
             for (int w = 0; w < kConsumerWarps; ++w) {
-                const float mw = ml_s[(w * GP + g) * 2];
+                const float mw = ml_s[(w * GS + g) * 2];
                 const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
-                Lsum += ml_s[(w * GP + g) * 2 + 1] * f;
-                O += o_s[(w * GP + g) * HD + d] * f;
+                Lsum += ml_s[(w * GS + g) * 2 + 1] * f;
+                O += o_s[(w * GS + g) * HD + d] * f;
             }
             if (whole) {
                 emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
-            } else if (JX_CHECKED(a, (slot + 1) * GP * (HD + 2) <= a.scratch_floats, 60, slot, seg, 0)) {
-                float* dst = a.scratch + (slot * GP + g) * (HD + 2);
+            } else if (JX_CHECKED(a, (slot + 1) * GS * (HD + 2) <= a.scratch_floats, 60, slot, seg, 0)) {
+                float* dst = a.scratch + (slot * GS + g) * (HD + 2);
                 dst[d] = O;
                 if (d == 0) {
                     dst[HD] = M;
@@ -605,12 +903,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float* ms = o_s;              // [np][G] piece maxima, then scale factors
                 float* ls = o_s + np * Gn;    // [np][G] piece sums
                 float* tot = ls + np * Gn;    // [G] merged max, [G] merged sum
-                const float* base_p = a.scratch + (c_first + seg) * GP * (HD + 2);
-                if ((2 * np + 2) * Gn <= kConsumerWarps * GP * HD) {
+                const float* base_p = a.scratch + (c_first + seg) * GS * (HD + 2);
+                if ((2 * np + 2) * Gn <= kConsumerWarps * GS * HD) {
                     // one parallel pass over every piece's (m, l) ...
                     for (int idx = ctid; idx < np * Gn; idx += kConsumerThreads) {
                         const int q = idx / Gn, g = idx % Gn;
-                        const float* src = base_p + (static_cast<long long>(q) * GP + g) * (HD + 2);
+                        const float* src = base_p + (static_cast<long long>(q) * GS + g) * (HD + 2);
                         ms[idx] = __ldcg(src + HD);
                         ls[idx] = __ldcg(src + HD + 1);
                     }
@@ -632,9 +930,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     named_bar_sync(1, kConsumerThreads);
                     // ... then o: every load of a chunk of pieces is issued before any
                     // is used (one round trip per chunk)
-                    constexpr int E = (GP * HD + kConsumerThreads - 1) / kConsumerThreads;
+                    constexpr int E = (GS * HD + kConsumerThreads - 1) / kConsumerThreads;
                     constexpr int QC = (32 / E) < 1 ? 1 : ((32 / E) > 8 ? 8 : (32 / E));
-                    const long long step = static_cast<long long>(GP) * (HD + 2);
+                    const long long step = static_cast<long long>(GS) * (HD + 2);
                     float O[E];
 #pragma unroll
                     for (int e = 0; e < E; ++e) O[e] = 0.0f;
@@ -674,10 +972,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int g = idx / HD, d = idx % HD;
                         float M = -INFINITY;
                         for (long long cc = c_first; cc <= c_last; ++cc)
-                            M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GP + g) * (HD + 2) + HD));
+                            M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GS + g) * (HD + 2) + HD));
                         float Lsum = 0.0f, O = 0.0f;
                         for (long long cc = c_first; cc <= c_last; ++cc) {
-                            const float* src = a.scratch + ((cc + seg) * GP + g) * (HD + 2);
+                            const float* src = a.scratch + ((cc + seg) * GS + g) * (HD + 2);
                             const float mw = __ldcg(src + HD);
                             const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
                             Lsum += __ldcg(src + HD + 1) * f;

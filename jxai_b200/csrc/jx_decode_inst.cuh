@@ -1,6 +1,7 @@
 // jx_decode_inst.cuh -- instantiates the decode kernel for one cache element
-// type (JX_INST_DT) over head_dim {32, 64, 128, 256} x group {1, 2, 4, 8} and
-// provides that type's dispatcher.  Included once by each jx_decode_<dt>.cu so
+// type (JX_INST_DT) over head_dim {32, 64, 128, 256} x group {1, 2, 4, 8}
+// (plus, for 16-bit caches, head_dim {32, 64} with two kv heads per tile row)
+// and provides that type's dispatcher.  Included once by each jx_decode_<dt>.cu so
 // the three element types compile in parallel.
 #include "jx_decode.cuh"
 
@@ -12,17 +13,17 @@ namespace jx {
 
 namespace {
 
-template <int HD, int GP>
+template <int HD, int GP, int KP>
 struct Entry {
     static constexpr int DT = JX_INST_DT;
-    static int smem(int stages) { return SmemLayout<HD, GP, DT>::total(stages); }
+    static int smem(int stages) { return SmemLayout<HD, GP, DT, KP>::total(stages); }
     static int occupancy(int stages) {
         const int bytes = smem(stages);
-        if (cudaFuncSetAttribute(decode_kernel<HD, GP, DT>,
+        if (cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
             return 0;
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<HD, GP, DT>, kThreads,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<HD, GP, DT, KP>, kThreads,
                                                           bytes) != cudaSuccess)
             return 0;
         return n;
@@ -35,17 +36,17 @@ struct Entry {
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= 64 || set_bytes[dev] < bytes) {
-            e = cudaFuncSetAttribute(decode_kernel<HD, GP, DT>,
+            e = cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) set_bytes[dev] = bytes;
         }
-        decode_kernel<HD, GP, DT><<<L.grid, kThreads, bytes, L.stream>>>(*L.tmK, *L.tmV, L.args);
+        decode_kernel<HD, GP, DT, KP><<<L.grid, kThreads, bytes, L.stream>>>(*L.tmK, *L.tmV, L.args);
         return cudaGetLastError();
     }
 };
 
-template <int HD>
+template <int HD, int KP>
 bool pick_gp(int gp, int op, int stages, const DecodeLaunch* L, int* out_i, cudaError_t* out_e) {
     auto run = [&](auto entry) {
         using E = decltype(entry);
@@ -54,21 +55,33 @@ bool pick_gp(int gp, int op, int stages, const DecodeLaunch* L, int* out_i, cuda
         else *out_e = E::launch(*L);
     };
     switch (gp) {
-        case 1: run(Entry<HD, 1>{}); return true;
-        case 2: run(Entry<HD, 2>{}); return true;
-        case 4: run(Entry<HD, 4>{}); return true;
-        case 8: run(Entry<HD, 8>{}); return true;
+        case 1: run(Entry<HD, 1, KP>{}); return true;
+        case 2: run(Entry<HD, 2, KP>{}); return true;
+        case 4: run(Entry<HD, 4, KP>{}); return true;
+        case 8: run(Entry<HD, 8, KP>{}); return true;
         default: return false;
     }
 }
 
-bool dispatch(int head_dim, int gp, int op, int stages, const DecodeLaunch* L, int* out_i,
-              cudaError_t* out_e) {
+bool dispatch(int head_dim, int gp, int kp, int op, int stages, const DecodeLaunch* L,
+              int* out_i, cudaError_t* out_e) {
+    if (kp == 2) {
+        if constexpr (JX_INST_DT == DT_F32) {
+            return false;
+        } else {
+            switch (head_dim) {
+                case 32: return pick_gp<32, 2>(gp, op, stages, L, out_i, out_e);
+                case 64: return pick_gp<64, 2>(gp, op, stages, L, out_i, out_e);
+                default: return false;
+            }
+        }
+    }
+    if (kp != 1) return false;
     switch (head_dim) {
-        case 32: return pick_gp<32>(gp, op, stages, L, out_i, out_e);
-        case 64: return pick_gp<64>(gp, op, stages, L, out_i, out_e);
-        case 128: return pick_gp<128>(gp, op, stages, L, out_i, out_e);
-        case 256: return pick_gp<256>(gp, op, stages, L, out_i, out_e);
+        case 32: return pick_gp<32, 1>(gp, op, stages, L, out_i, out_e);
+        case 64: return pick_gp<64, 1>(gp, op, stages, L, out_i, out_e);
+        case 128: return pick_gp<128, 1>(gp, op, stages, L, out_i, out_e);
+        case 256: return pick_gp<256, 1>(gp, op, stages, L, out_i, out_e);
         default: return false;
     }
 }
@@ -78,9 +91,9 @@ bool dispatch(int head_dim, int gp, int op, int stages, const DecodeLaunch* L, i
 #define JX_CAT2(a, b) a##b
 #define JX_CAT(a, b) JX_CAT2(a, b)
 
-bool JX_CAT(decode_dispatch_dt, JX_INST_DT)(int head_dim, int gp, int op, int stages,
+bool JX_CAT(decode_dispatch_dt, JX_INST_DT)(int head_dim, int gp, int kp, int op, int stages,
                                            const DecodeLaunch* L, int* out_i, cudaError_t* out_e) {
-    return dispatch(head_dim, gp, op, stages, L, out_i, out_e);
+    return dispatch(head_dim, gp, kp, op, stages, L, out_i, out_e);
 }
 
 }  // namespace jx

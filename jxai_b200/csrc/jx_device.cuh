@@ -157,6 +157,12 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (TMA) writes of the same bytes.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Atomic add with acquire-release semantics at GPU scope.  Issued by one
 // thread after a CTA barrier, it publishes every write the CTA made before the
 // barrier and observes every write published by earlier arrivals.
@@ -254,6 +260,65 @@ __device__ __forceinline__ void unpack16(const uint4& r, float* out) {
                 out[2 * i + 1] = f16_bits_to_f32(w[i] >> 16);
             }
         }
+    }
+}
+
+// ---------------------------------------------------------------- warp MMA (16-bit caches)
+// m16n8k16 with fp32 accumulation; A row-major, B column-major.  Lane L holds
+// A rows L/4 and L/4+8, B column L/4 and C rows L/4, L/4+8 (columns 2(L%4), +1).
+template <int DT>
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    if constexpr (DT == DT_BF16) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+            "{%8,%9}, {%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+// Four 8x8 16-bit matrices from shared memory; lane L supplies the address of
+// row L%8 of matrix L/8.  `trans` delivers each matrix transposed.
+template <bool trans>
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+    if constexpr (trans)
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                     : "r"(addr));
+    else
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                     : "r"(addr));
+}
+
+// Transposes an 8x8 16-bit matrix held one row pair per lane (lane L: row
+// L/4, columns 2(L%4), 2(L%4)+1) into the same layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+// Two floats as a 16-bit pair (x in the low half) rounded to nearest, plus the
+// pair of what the rounding left over: x = hi + lo to ~2^-16 relative.
+template <int DT>
+__device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint32_t& lo) {
+    if constexpr (DT == DT_BF16) {
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(y), "f"(x));
+        const float xh = __uint_as_float(hi << 16), yh = __uint_as_float(hi & 0xFFFF0000u);
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(y - yh), "f"(x - xh));
+    } else {
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(y), "f"(x));
+        const float xh = f16_bits_to_f32(hi & 0xFFFFu), yh = f16_bits_to_f32(hi >> 16);
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(y - yh), "f"(x - xh));
     }
 }
 

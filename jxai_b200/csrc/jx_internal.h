@@ -54,7 +54,8 @@ struct DecodeArgs {
     float* part_out; // partial mode output, or null
     int* err;        // device error word
     int n_stages;
-    int n_consumers; // consumer warps that take tiles (1..4); n_stages % n_consumers == 0
+    int n_consumers; // consumer warps that take tiles (1..4), a multiple of the warps per
+                     // tile (kv heads per tile row); n_stages % (warps / per tile) == 0
     // extents, used by the optional device-side checks (JX_DEVICE_CHECKS builds)
     long long n_io;          // rows of q/k/v/out
     long long cache_elems;   // elements of K (and of V)
@@ -75,23 +76,34 @@ struct DecodeLaunch {
     const CUtensorMap* tmV;
     int head_dim;
     int gp;      // padded group size (1, 2, 4, 8)
+    int kp;      // kv heads per tile row (kv_pack)
     int dtype;   // 0 f32, 1 bf16, 2 f16 trunc
     int grid;
     int stages;
     cudaStream_t stream;
 };
 
-// Dynamic shared memory bytes of the kernel for (head_dim, gp, dtype, stages),
-// or -1 when that combination is not compiled.
-int decode_smem_bytes(int head_dim, int gp, int dtype, int stages);
+// kv heads that share one tile row: 2 for 16-bit caches whose kv-head rows
+// are under 256 bytes (head_dim 32, 64) when the heads pair up evenly and the
+// query group needs no padding, 1 otherwise.  With 2, each tile row the TMA
+// fetches is one contiguous run over two kv heads (256 bytes at head_dim 64);
+// separate 128-byte runs at a 1 KB row stride cost ~1.5x their bytes in DRAM
+// traffic on B200.  A segment then covers kp kv heads and kp*G query heads,
+// and each tile goes to kp consumer warps, one per kv head.
+inline int kv_pack(int head_dim, int esz, unsigned n_kv, unsigned G, int gp) {
+    return (esz == 2 && head_dim * esz < 256 && n_kv % 2 == 0 && static_cast<int>(G) == gp) ? 2 : 1;
+}
+// Dynamic shared memory bytes of the kernel for (head_dim, gp, kp, dtype,
+// stages), or -1 when that combination is not compiled.
+int decode_smem_bytes(int head_dim, int gp, int kp, int dtype, int stages);
 // Resident CTAs per SM for that configuration (occupancy calculator).
-int decode_ctas_per_sm(int head_dim, int gp, int dtype, int stages);
+int decode_ctas_per_sm(int head_dim, int gp, int kp, int dtype, int stages);
 // Launches; returns a cudaError_t.
 cudaError_t decode_launch(const DecodeLaunch& L);
-// Consumer warps for a ring of `stages` (a divisor of it, at most 4).
-int consumers_for(int stages);
+// Consumer warps for a ring of `stages` with `split` warps per tile.
+int consumers_for(int stages, int split);
 // Default ring depth and CTAs per SM for one kernel configuration.
-void default_shape(int hd, int gp, int dtype, int* stages, int* cps);
+void default_shape(int hd, int gp, int kp, int dtype, int* stages, int* cps);
 // Sets the calling thread's jx_last_error_string() message.
 void set_last_error(const char* msg);
 // (cos, sin) of every rotated pair at `pos`, as apply_rope computes them;

@@ -21,38 +21,39 @@
 #include "jx_internal.h"
 
 namespace jx {
-bool decode_dispatch_dt0(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
-bool decode_dispatch_dt1(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
-bool decode_dispatch_dt2(int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+bool decode_dispatch_dt0(int, int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+bool decode_dispatch_dt1(int, int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
+bool decode_dispatch_dt2(int, int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
 
-static bool dispatch(int dtype, int hd, int gp, int op, int stages, const DecodeLaunch* L,
+static bool dispatch(int dtype, int hd, int gp, int kp, int op, int stages, const DecodeLaunch* L,
                      int* oi, cudaError_t* oe) {
     switch (dtype) {
-        case 0: return decode_dispatch_dt0(hd, gp, op, stages, L, oi, oe);
-        case 1: return decode_dispatch_dt1(hd, gp, op, stages, L, oi, oe);
-        case 2: return decode_dispatch_dt2(hd, gp, op, stages, L, oi, oe);
+        case 0: return decode_dispatch_dt0(hd, gp, kp, op, stages, L, oi, oe);
+        case 1: return decode_dispatch_dt1(hd, gp, kp, op, stages, L, oi, oe);
+        case 2: return decode_dispatch_dt2(hd, gp, kp, op, stages, L, oi, oe);
         default: return false;
     }
 }
 
-int decode_smem_bytes(int hd, int gp, int dtype, int stages) {
+int decode_smem_bytes(int hd, int gp, int kp, int dtype, int stages) {
     int v = -1;
     cudaError_t e = cudaSuccess;
-    if (!dispatch(dtype, hd, gp, 0, stages, nullptr, &v, &e)) return -1;
+    if (!dispatch(dtype, hd, gp, kp, 0, stages, nullptr, &v, &e)) return -1;
     return v;
 }
 
-int decode_ctas_per_sm(int hd, int gp, int dtype, int stages) {
+int decode_ctas_per_sm(int hd, int gp, int kp, int dtype, int stages) {
     int v = 0;
     cudaError_t e = cudaSuccess;
-    if (!dispatch(dtype, hd, gp, 1, stages, nullptr, &v, &e)) return 0;
+    if (!dispatch(dtype, hd, gp, kp, 1, stages, nullptr, &v, &e)) return 0;
     return v;
 }
 
 cudaError_t decode_launch(const DecodeLaunch& L) {
     int v = 0;
     cudaError_t e = cudaErrorInvalidValue;
-    if (!dispatch(L.dtype, L.head_dim, L.gp, 2, L.stages, &L, &v, &e)) return cudaErrorInvalidValue;
+    if (!dispatch(L.dtype, L.head_dim, L.gp, L.kp, 2, L.stages, &L, &v, &e))
+        return cudaErrorInvalidValue;
     return e;
 }
 
@@ -118,29 +119,30 @@ __global__ void fill_f32_kernel(float* dst, uint64_t n, uint64_t seed, uint32_t 
         dst[i] = normal_at(seed, stream_id, i);
 }
 
-// Consumer warps that take tiles for a ring of `stages`: every stage must be
-// consumed by one warp only, so the count divides the ring size.
-int consumers_for(int stages) {
-    for (int c = 4; c > 1; --c)
-        if (stages % c == 0) return c;
-    return 1;
+// Consumer warps for a ring of `stages` when `split` warps share each tile:
+// every stage must be consumed by one group of warps only, so the number of
+// tile streams (warps / split) divides the ring size.
+int consumers_for(int stages, int split) {
+    for (int c = 4; c >= split; --c)
+        if (c % split == 0 && stages % (c / split) == 0) return c;
+    return split;
 }
 
 // Default pipeline depth / residency for one kernel configuration: a ring of
 // 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if it
 // fits, else with one CTA per SM, else the deepest ring that fits one CTA.
-void default_shape(int hd, int gp, int dtype, int* stages, int* cps) {
+void default_shape(int hd, int gp, int kp, int dtype, int* stages, int* cps) {
     const int per_sm = 227 * 1024;
     for (int c = 2; c >= 1; --c)
         for (int ns : {8, 4})
-            if (decode_smem_bytes(hd, gp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
+            if (decode_smem_bytes(hd, gp, kp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
                 *stages = ns;
                 *cps = c;
                 return;
             }
     int best = 2;
     for (int ns = 7; ns >= 2; --ns)
-        if (decode_smem_bytes(hd, gp, dtype, ns) <= per_sm) { best = ns; break; }
+        if (decode_smem_bytes(hd, gp, kp, dtype, ns) <= per_sm) { best = ns; break; }
     *stages = best;
     *cps = 1;
 }
@@ -500,7 +502,9 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     for (size_t gi = 0; gi < groups.size(); ++gi) {
         const Group& grp = groups[gi];
         const int hd = grp.hd;
-        const int box_kind = hd * kv->esz >= 128 ? 0 : 1;
+        const int kp = kv_pack(hd, kv->esz, a->n_kv_heads, G, gp);
+        const uint32_t n_kv = a->n_kv_heads / kp;  // segments per (sequence, layer) pair
+        const int box_kind = kp * hd * kv->esz >= 128 ? 0 : 1;
         int rc = encode_maps(kv, box_kind);
         if (rc) return rc;
         // ---- pairs and rope rows
@@ -561,7 +565,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 }
                 pr.rope_row = rid;
                 pairs.push_back(pr);
-                off += len * a->n_kv_heads;
+                off += len * n_kv;
             }
         }
         const long long total = off;
@@ -579,23 +583,23 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                                 pr.seq >= 0 && pr.seq < static_cast<int>(D.n_seqs) &&
                                 pr.rope_half >= 0 && pr.rope_half <= hd / 2;
                 if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent work plan row");
-                o += static_cast<long long>(pr.len) * a->n_kv_heads;
+                o += static_cast<long long>(pr.len) * n_kv;
             }
         }
         // ---- launch shape (cached per configuration)
         int stages = 0, cps = 0;
-        const auto skey = std::make_tuple(hd, gp, kv->opt_stages, kv->opt_ctas_per_sm);
+        const auto skey = std::make_tuple(hd, gp * 16 + kp, kv->opt_stages, kv->opt_ctas_per_sm);
         auto sit = kv->shapes.find(skey);
         if (sit != kv->shapes.end()) {
             stages = sit->second.first;
             cps = sit->second.second;
         } else {
-            default_shape(hd, gp, D.dtype, &stages, &cps);
+            default_shape(hd, gp, kp, D.dtype, &stages, &cps);
             if (kv->opt_stages) stages = kv->opt_stages;
-            if (decode_smem_bytes(hd, gp, D.dtype, stages) < 0)
+            if (decode_smem_bytes(hd, gp, kp, D.dtype, stages) < 0)
                 return fail(JX_ERR_UNSUPPORTED, "no kernel for head_dim %d group %d dtype %d", hd,
                             gp, D.dtype);
-            const int occ = decode_ctas_per_sm(hd, gp, D.dtype, stages);
+            const int occ = decode_ctas_per_sm(hd, gp, kp, D.dtype, stages);
             if (occ <= 0)
                 return fail(JX_ERR_UNSUPPORTED, "kernel does not fit with %d stages", stages);
             if (kv->opt_ctas_per_sm) cps = kv->opt_ctas_per_sm;
@@ -627,8 +631,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         std::memcpy(bytes.data() + cta_off, cta_pair.data(), cta_pair.size() * sizeof(int));
         rc = upload_plan(kv, gi, bytes, stream);
         if (rc) return rc;
-        const long long n_segs = static_cast<long long>(pairs.size()) * a->n_kv_heads;
-        rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * (hd + 2),
+        const long long n_segs = static_cast<long long>(pairs.size()) * n_kv;
+        rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * kp * (hd + 2),
                             static_cast<size_t>(std::max<long long>(n_segs, 1)));
         if (rc) return rc;
 
@@ -638,8 +642,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.cta_pair = reinterpret_cast<const int*>(static_cast<unsigned char*>(kv->slots[gi].d_buf) +
                                                   cta_off);
         A.n_pairs = static_cast<int>(pairs.size());
-        A.n_kv = static_cast<int>(a->n_kv_heads);
-        A.G = static_cast<int>(G);
+        A.n_kv = static_cast<int>(n_kv);
+        A.G = static_cast<int>(G) * kp;
         A.n_heads = static_cast<int>(a->n_heads);
         A.total = total;
         A.q = a->q;
@@ -664,7 +668,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.part_out = partial ? partials : nullptr;
         A.err = kv->d_err;
         A.n_stages = stages;
-        A.n_consumers = consumers_for(stages);
+        A.n_consumers = consumers_for(stages, kp);
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;
         A.scratch_floats = static_cast<long long>(kv->scratch_floats);
@@ -673,12 +677,13 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.capacity = static_cast<int>(D.capacity);
         A.n_cache_layers = static_cast<int>(D.n_layers);
         A.n_cache_seqs = static_cast<int>(D.n_seqs);
-        A.smem_bytes = decode_smem_bytes(hd, gp, D.dtype, stages);
+        A.smem_bytes = decode_smem_bytes(hd, gp, kp, D.dtype, stages);
         A.dbg = kv->d_dbg;
         Lc.tmK = &kv->tmK[box_kind];
         Lc.tmV = &kv->tmV[box_kind];
         Lc.head_dim = hd;
         Lc.gp = gp;
+        Lc.kp = kp;
         Lc.dtype = D.dtype;
         Lc.grid = static_cast<int>(P);
         Lc.stages = stages;

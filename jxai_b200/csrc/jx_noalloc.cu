@@ -112,6 +112,8 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
         return nfail(JX_ERR_UNSUPPORTED, "head_dim %u (compiled: 32, 64, 128, 256)", hd);
     if (hd * esz < 64) return nfail(JX_ERR_UNSUPPORTED, "head rows below 64 bytes");
+    const int kp = kv_pack(static_cast<int>(hd), static_cast<int>(esz), a->n_kv_heads, G, gp);
+    const uint32_t n_kv = a->n_kv_heads / kp;  // segments per (sequence, layer) pair
     if (static_cast<uint64_t>(a->n_kv_heads) * hd > D.row_stride ||
         a->q_stride < a->n_heads * hd || a->kv_stride < a->n_kv_heads * hd)
         return nfail(JX_ERR_INVALID, "strides smaller than the layer's rows");
@@ -208,7 +210,7 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
                          rope + static_cast<size_t>(rid) * width, width);
             }
             pr.rope_row = rid;
-            off += static_cast<long long>(pr.len) * a->n_kv_heads;
+            off += static_cast<long long>(pr.len) * n_kv;
         }
     }
     const long long total = off;
@@ -216,8 +218,8 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
 
     // ---- launch shape and scratch layout
     int stages = 0, cps = 0;
-    default_shape(static_cast<int>(hd), gp, D.dtype, &stages, &cps);
-    const int occ = decode_ctas_per_sm(static_cast<int>(hd), gp, D.dtype, stages);
+    default_shape(static_cast<int>(hd), gp, kp, D.dtype, &stages, &cps);
+    const int occ = decode_ctas_per_sm(static_cast<int>(hd), gp, kp, D.dtype, stages);
     if (occ <= 0) return nfail(JX_ERR_UNSUPPORTED, "kernel does not fit");
     cps = std::max(1, std::min(cps, occ));
     int sms = 0;
@@ -225,10 +227,10 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
         return nfail(JX_ERR_CUDA, "cannot query the SM count");
     long long P = std::min<long long>(static_cast<long long>(sms) * cps,
                                       std::max<long long>(1, (total + 63) / 64));
-    const long long n_segs = static_cast<long long>(n_pairs) * a->n_kv_heads;
+    const long long n_segs = static_cast<long long>(n_pairs) * n_kv;
     const size_t counters_off = kHeaderBytes;
     const size_t partials_off = round_up(counters_off + static_cast<size_t>(n_segs) * 4, 256);
-    const size_t partial_floats = static_cast<size_t>(P + n_segs) * gp * (hd + 2);
+    const size_t partial_floats = static_cast<size_t>(P + n_segs) * gp * kp * (hd + 2);
     const size_t plan_off = round_up(partials_off + partial_floats * 4, 256);
     const size_t need = plan_off + plan_bytes;
     if (need > kNoAllocScratchBytes)
@@ -241,7 +243,7 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     auto enc = encoder();
     if (!enc) return nfail(JX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
     CUtensorMap tmK, tmV;
-    const uint32_t box_bytes = hd * esz >= 128 ? 128 : 64;
+    const uint32_t box_bytes = kp * hd * esz >= 128 ? 128 : 64;
     const cuuint64_t dims[4] = {D.row_stride, D.capacity, D.n_layers, D.n_seqs};
     const cuuint64_t strides[3] = {
         static_cast<cuuint64_t>(D.row_stride) * esz,
@@ -272,8 +274,8 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     DecodeArgs& A = Lc.args;
     A.pairs = reinterpret_cast<const PairRow*>(scratch + plan_off);
     A.n_pairs = static_cast<int>(n_pairs);
-    A.n_kv = static_cast<int>(a->n_kv_heads);
-    A.G = static_cast<int>(G);
+    A.n_kv = static_cast<int>(n_kv);
+    A.G = static_cast<int>(G) * kp;
     A.n_heads = static_cast<int>(a->n_heads);
     A.total = total;
     A.q = a->q;
@@ -298,7 +300,7 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     A.err = reinterpret_cast<int*>(scratch);
     A.dbg = reinterpret_cast<int*>(scratch) + 8;
     A.n_stages = stages;
-    A.n_consumers = consumers_for(stages);
+    A.n_consumers = consumers_for(stages, kp);
     A.n_io = static_cast<long long>(n_pairs);
     A.cache_elems = A.seq_stride * D.n_seqs;
     A.scratch_floats = static_cast<long long>(partial_floats);
@@ -307,11 +309,12 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     A.capacity = static_cast<int>(D.capacity);
     A.n_cache_layers = static_cast<int>(D.n_layers);
     A.n_cache_seqs = static_cast<int>(D.n_seqs);
-    A.smem_bytes = decode_smem_bytes(static_cast<int>(hd), gp, D.dtype, stages);
+    A.smem_bytes = decode_smem_bytes(static_cast<int>(hd), gp, kp, D.dtype, stages);
     Lc.tmK = &tmK;
     Lc.tmV = &tmV;
     Lc.head_dim = static_cast<int>(hd);
     Lc.gp = gp;
+    Lc.kp = kp;
     Lc.dtype = D.dtype;
     Lc.grid = static_cast<int>(P);
     Lc.stages = stages;

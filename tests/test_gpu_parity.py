@@ -25,7 +25,7 @@ def _torch():
 
 def run_case(dtype, n_heads, n_kv, hd, lengths, neox=True, n_layers=2, softcap=0.0, window=0,
              swa_layers=(), grid=0, seed=0, capacity=None, row_pad=0, rope_dim=None,
-             yarn=1.0, rope_freqs=None, check_fp32_ref=False):
+             yarn=1.0, rope_freqs=None, check_fp32_ref=False, q_scale=1.0, poison_tail=False):
     import jxai_b200 as jx
     torch = _torch()
     rng = np.random.default_rng(seed)
@@ -37,10 +37,16 @@ def run_case(dtype, n_heads, n_kv, hd, lengths, neox=True, n_layers=2, softcap=0
                        rope_freqs=rope_freqs) for l in range(n_layers)]
     kc = random_cache(rng, (n_seqs, n_layers, cap, rs), dtype)
     vc = random_cache(rng, (n_seqs, n_layers, cap, rs), dtype)
-    q = rng.standard_normal((n_seqs, n_layers, n_heads * hd)).astype(np.float32)
+    q = (rng.standard_normal((n_seqs, n_layers, n_heads * hd)) * q_scale).astype(np.float32)
     k = rng.standard_normal((n_seqs, n_layers, n_kv * hd)).astype(np.float32)
     v = rng.standard_normal((n_seqs, n_layers, n_kv * hd)).astype(np.float32)
     pos = [T - 1 for T in lengths]
+    if poison_tail:
+        # rows past each sequence's position are never attended; make them Inf
+        inf = {F32: np.float32(np.inf), BF16: np.uint16(0x7F80), F16T: np.uint16(0x7C00)}[dtype]
+        for s_, T in enumerate(lengths):
+            kc[s_, :, T:] = inf
+            vc[s_, :, T:] = inf
     scale = 1.0 / math.sqrt(hd)
 
     cache = jx.KVCache(n_seqs, n_layers, cap, rs, dtype)
@@ -102,6 +108,32 @@ def test_head_dim_32_and_group_8():
     run_case(F16T, 4, 2, 32, [40, 7])           # toy-model shape (fp16 trunc, native)
     run_case(BF16, 8, 1, 64, [70])              # group 8
     run_case(F32, 7, 1, 64, [70])               # group 7 padded to 8
+
+
+@pytest.mark.parametrize("dtype", [BF16, F16T])
+@pytest.mark.parametrize("shape", [(8, 8, 64), (16, 8, 64), (16, 2, 64), (8, 8, 32), (6, 3, 64),
+                                   (16, 4, 128), (8, 1, 256), (12, 4, 64)])
+def test_16bit_tensor_core_path(dtype, shape):
+    # 16-bit caches run QK and PV on the tensor cores, two kv heads per tile row
+    # when the heads pair up (head_dim 32/64, even kv heads, unpadded group);
+    # grid=5 splits segments into pieces merged across CTAs
+    H, HK, hd = shape
+    run_case(dtype, H, HK, hd, [1, 17, 32, 33, 300], grid=5, n_layers=2)
+
+
+@pytest.mark.parametrize("dtype", [BF16, F16T])
+def test_16bit_softcap_window_and_q_range(dtype):
+    run_case(dtype, 8, 2, 64, [600, 100], softcap=50.0, window=64, swa_layers=(0,), n_layers=3)
+    run_case(dtype, 8, 2, 64, [300, 5], q_scale=3e4)     # |q| beyond the fp16 range
+    run_case(dtype, 8, 2, 64, [300, 5], q_scale=1e-6)    # |q| in the fp16 subnormals
+    run_case(dtype, 4, 2, 128, [300, 5], q_scale=3e4)
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16, F16T])
+def test_unattended_rows_holding_inf(dtype):
+    # the tail tile of a segment reaches rows past pos; Inf there must not leak
+    run_case(dtype, 32, 8, 64, [33, 47, 5], capacity=96, poison_tail=True, grid=3)
+    run_case(dtype, 4, 1, 256, [40], capacity=64, poison_tail=True)
 
 
 def test_softcap_and_window():
