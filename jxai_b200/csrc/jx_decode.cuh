@@ -75,17 +75,21 @@ template <int HD, int GP, int DT, int KP = 1>
 struct SmemLayout {
     using G = Geo<HD * KP, DT>;
     static constexpr int GS = GP * KP;
-    static constexpr int q_bytes = GS * HD * 4;
+    static constexpr int q_bytes = GS * HD * 4;       // rotated q of the current piece
+    static constexpr int qraw_bytes = 2 * GS * HD * 4;  // raw q of two pieces (bulk copies)
+    static constexpr int rope_bytes = 2 * HD * 4;       // (cos, sin) rows of two pieces
     static constexpr int p_bytes = DT == DT_F32 ? kConsumerWarps * kTileRows * GS * 4 : 0;
     static constexpr int o_bytes = kConsumerWarps * GS * HD * 4;
     static constexpr int ml_bytes = kConsumerWarps * GS * 2 * 4;
-    static constexpr int misc_bytes = 16;
+    static constexpr int misc_bytes = 16 + 2 * 32;      // flags + two split-piece records
+    static constexpr int n_extra_bars = 4;              // q full[2], q empty[2]
     static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
     static __host__ __device__ constexpr int bars_offset(int ns) {
-        return stages_bytes(ns) + q_bytes + p_bytes + o_bytes + ml_bytes + misc_bytes;
+        return stages_bytes(ns) + q_bytes + qraw_bytes + rope_bytes + p_bytes + o_bytes +
+               ml_bytes + misc_bytes;
     }
     static __host__ __device__ constexpr int total(int ns) {
-        return bars_offset(ns) + ns * 2 * 8 + 1024;  // + alignment slack
+        return bars_offset(ns) + (ns * 2 + n_extra_bars) * 8 + 1024;  // + alignment slack
     }
 };
 
@@ -192,19 +196,98 @@ __device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow&
 // Writes one merged (g, d) element of a finished segment: normalised output,
 // or the partial (o, m, l) in partial mode.
 template <int HD>
-__device__ __forceinline__ void emit_final(const DecodeArgs& a, const PairRow& pr, int h, int d,
-                                           float M, float L, float O) {
-    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && h < a.n_heads && d < HD, 20, pr.io, h, d))
-        return;
+__device__ __forceinline__ void emit_final(const DecodeArgs& a, int io, int h, int d, float M,
+                                           float L, float O) {
+    if (!JX_CHECKED(a, io >= 0 && io < a.n_io && h < a.n_heads && d < HD, 20, io, h, d)) return;
     if (a.part_out) {
-        const long long base = (static_cast<long long>(pr.io) * a.n_heads + h) * (HD + 2);
+        const long long base = (static_cast<long long>(io) * a.n_heads + h) * (HD + 2);
         a.part_out[base + d] = O;
         if (d == 0) {
             a.part_out[base + HD] = M;
             a.part_out[base + HD + 1] = L;
         }
     } else {
-        a.out[static_cast<long long>(pr.io) * a.q_stride + h * HD + d] = O * (1.0f / L);
+        a.out[static_cast<long long>(io) * a.q_stride + h * HD + d] = O * (1.0f / L);
+    }
+}
+
+// A piece that is not a whole segment.  Its partial (o, m, l) goes to scratch
+// slot (cta + seg) when the piece ends and the CTA counts it in on the
+// segment's counter -- at once (release only, nobody waits) when more pieces
+// follow in the CTA, else after the CTA's last piece.  The CTA that counts in
+// last merges the segment after its last piece.
+struct SplitRec {
+    long long seg;        // segment index: pair * n_kv + kv head (of the segment)
+    long long seg_start;  // flattened index of the segment's first row
+    int len;              // segment rows
+    int io;               // q/out row of the pair
+    int kvh;              // kv head (of the segment) within the pair
+    int early;            // 1: counted in when the piece ended (more pieces followed)
+};
+static_assert(sizeof(SplitRec) == 32, "SplitRec layout");
+
+// Last-arriver merge of segment `r`: the partials of CTAs c_first..c_last are
+// combined by log-sum-exp and the output written.  Each consumer thread owns
+// E (head, dim) elements and issues the loads of QC pieces for all of them
+// before using any (one round trip per QC pieces); no barriers.  Inlined: a
+// call would give the kernel a stack frame, which measurably slows launches.
+template <int HD, int GS>
+__device__ __forceinline__ void merge_split(const DecodeArgs& a, const SplitRec& r, long long c_first,
+                                         long long c_last, int ctid) {
+    constexpr int E = (GS * HD + kConsumerThreads - 1) / kConsumerThreads;
+    constexpr int QC = (24 / E) < 1 ? 1 : ((24 / E) > 8 ? 8 : (24 / E));
+    const int np = static_cast<int>(c_last - c_first + 1);
+    const int Gn = a.G;
+    const long long step = static_cast<long long>(GS) * (HD + 2);
+    const float* base_p = a.scratch + (c_first + r.seg) * step;
+    float M[E], Ls[E], O[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        M[e] = -INFINITY;
+        Ls[e] = 0.0f;
+        O[e] = 0.0f;
+    }
+    for (int q0 = 0; q0 < np; q0 += QC) {
+        float mv[E][QC], lv[E][QC], ov[E][QC];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const int idx = ctid + e * kConsumerThreads;
+            const int g = idx / HD, d = idx % HD;
+            const float* src = base_p + static_cast<long long>(g) * (HD + 2);
+#pragma unroll
+            for (int qq = 0; qq < QC; ++qq) {
+                const bool ok = idx < Gn * HD && q0 + qq < np;
+                const float* pq = src + (q0 + qq) * step;
+                mv[e][qq] = ok ? __ldcg(pq + HD) : -INFINITY;
+                lv[e][qq] = ok ? __ldcg(pq + HD + 1) : 0.0f;
+                ov[e][qq] = ok ? __ldcg(pq + d) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            float Mn = M[e];
+#pragma unroll
+            for (int qq = 0; qq < QC; ++qq) Mn = fmaxf(Mn, mv[e][qq]);
+            if (Mn == -INFINITY) continue;
+            const float f0 = M[e] == -INFINITY ? 0.0f : ex2_approx((M[e] - Mn) * kLog2e);
+            Ls[e] *= f0;
+            O[e] *= f0;
+#pragma unroll
+            for (int qq = 0; qq < QC; ++qq) {
+                const float f = mv[e][qq] == -INFINITY ? 0.0f : ex2_approx((mv[e][qq] - Mn) * kLog2e);
+                Ls[e] += lv[e][qq] * f;
+                O[e] += ov[e][qq] * f;
+            }
+            M[e] = Mn;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int idx = ctid + e * kConsumerThreads;
+        if (idx < Gn * HD) {
+            const int g = idx / HD, d = idx % HD;
+            emit_final<HD>(a, r.io, r.kvh * Gn + g, d, M[e], Ls[e], O[e]);
+        }
     }
 }
 
@@ -470,8 +553,22 @@ struct MmaWarp {
     }
 };
 
+// Register cap per configuration.  A 5-warp CTA pair puts three warps on
+// some SM sub-partition (16K registers each), so two CTAs per SM need at most
+// 170 registers per thread; configurations whose shared memory allows two
+// CTAs are held to 168, the others may use all 255.  (The tensor-core
+// consumer at head_dim 128 and group 8 would spill under the cap: it runs one
+// CTA per SM with a deeper ring instead.)
 template <int HD, int GP, int DT, int KP>
-__global__ void __launch_bounds__(kThreads, 1)
+struct RegCap {
+    static constexpr bool two_ctas =
+        SmemLayout<HD, GP, DT, KP>::total(4) + 1024 <= (227 * 1024) / 2 &&
+        !(DT != DT_F32 && HD >= 128 && GP * KP >= 8);
+    static constexpr int value = two_ctas ? 168 : 255;
+};
+
+template <int HD, int GP, int DT, int KP>
+__global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>::value))
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const DecodeArgs a) {
     constexpr int RW = HD * KP;  // tile row width (elements): KP kv heads side by side
@@ -487,16 +584,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* base = smem_raw + (base_u32 - raw_u32);
     const int NS = a.n_stages;
     float* q_s = reinterpret_cast<float*>(base + L::stages_bytes(NS));
-    float* p_s = q_s + L::q_bytes / 4;
+    float* qraw_s = q_s + L::q_bytes / 4;                                  // [2][GS*HD]
+    float2* rope_s = reinterpret_cast<float2*>(qraw_s + L::qraw_bytes / 4);  // [2][HD/2]
+    float* p_s = reinterpret_cast<float*>(rope_s) + L::rope_bytes / 4;
     float* o_s = p_s + L::p_bytes / 4;
     float* ml_s = o_s + L::o_bytes / 4;
-    int* misc = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);
-    const uint32_t bars = base_u32 + L::bars_offset(NS);  // full[s] at bars+8s, empty[s] at bars+8(NS+s)
+    int* misc = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);  // [1] abort, [2..3] last flags
+    SplitRec* recs = reinterpret_cast<SplitRec*>(misc + 4);     // [2]
+    // full[s] at bars+8s, empty[s] at bars+8(NS+s), q full[2], q empty[2] after them
+    const uint32_t bars = base_u32 + L::bars_offset(NS);
+    const uint32_t qfull = bars + 8 * (2 * NS);
+    const uint32_t qempty = qfull + 16;
     volatile int* abort_flag = misc + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) + 16 * NS <= a.smem_bytes &&
+    if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) +
+                               8 * (2 * NS + L::n_extra_bars) <= a.smem_bytes &&
                            a.n_consumers >= kSplit && a.n_consumers <= kConsumerWarps &&
                            a.n_consumers % kSplit == 0 && NS % (a.n_consumers / kSplit) == 0,
                     1, a.smem_bytes, NS, a.n_consumers))
@@ -506,6 +610,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < NS; ++s) {
             mbar_init(bars + 8 * s, 1);
             mbar_init(bars + 8 * (NS + s), kSplit);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(qfull + 8 * s, 1);
+            mbar_init(qempty + 8 * s, 1);
         }
         misc[0] = 0;
         misc[1] = 0;
@@ -540,6 +648,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                                    pr.row0 + pr.len <= a.capacity,
                             30, it.kvh, pr.cache_layer, pr.row0 + pr.len))
                 break;
+            // this piece's raw q (the segment's query heads) and (cos, sin) row
+            // -> q slot piece % 2, ahead of the consumers that rotate it
+            if (a.q_bulk) {
+                const int qs = piece & 1;
+                if (piece >= 2)
+                    mbar_wait_bounded(qempty + 8 * qs, ((piece >> 1) & 1) ^ 1u, abort_flag, a.err,
+                                      a.dbg, 4, piece);
+                if (lane == 0 && *abort_flag == 0 &&
+                    JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
+                                      pr.rope_row < a.n_rope_rows &&
+                                      (it.kvh + 1) * a.G <= a.n_heads,
+                               32, pr.io, pr.rope_row, it.kvh)) {
+                    const uint32_t qb = static_cast<uint32_t>(a.G) * HD * 4;
+                    mbar_arrive_expect_tx(qfull + 8 * qs, qb + HD * 4);
+                    bulk_load(smem_u32(qraw_s + qs * GS * HD),
+                              a.q + static_cast<long long>(pr.io) * a.q_stride +
+                                  static_cast<long long>(it.kvh) * a.G * HD,
+                              qb, qfull + 8 * qs);
+                    bulk_load(smem_u32(rope_s + qs * (HD / 2)),
+                              a.rope + static_cast<long long>(pr.rope_row) * (HD / 2), HD * 4,
+                              qfull + 8 * qs);
+                } else if (lane == 0) {
+                    mbar_arrive(qfull + 8 * qs);  // complete the phase without data
+                }
+                __syncwarp();
+            }
             // Tile holding the segment's newest row, when this piece holds it; the
             // row is stored (and fenced) before that tile is loaded.  In the CTA's
             // first piece -- the kernel's ramp, ring empty -- that is just before
@@ -604,6 +738,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = first; k < n_issued; ++k)
             mbar_wait_bounded(bars + 8 * (k % NS), (k / NS) & 1, abort_flag, a.err, a.dbg, 3, k,
                               false, kDrainLimitCycles);
+        if (a.q_bulk)
+            for (int k = piece > 2 ? piece - 2 : 0; k < piece; ++k)
+                mbar_wait_bounded(qfull + 8 * (k & 1), (k >> 1) & 1, abort_flag, a.err, a.dbg, 6,
+                                  k, false, kDrainLimitCycles);
         return;
     }
 
@@ -640,11 +778,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float inv_cap = a.inv_softcap;
     using MW = MmaWarp<HD, GP, (kMma ? DT : DT_BF16), KP>;
     MW mw;
+    int cpiece = 0;       // pieces started
+    int n_split = 0;      // pieces recorded in recs[]
+    int early_prev = -1;  // thread 0: counter value before an early count-in
+    long long pending_seg = -1;  // segment of an early count-in not issued yet
     while (it.next()) {
         const PairRow& pr = it.pr;
         const int kvh = it.kvh;
 
-        // q rotation for this segment's query group -> q_s (padded heads = 0)
+        // q rotation for this segment's query group -> q_s (padded heads = 0).
+        // Every reader of q_s for the previous piece passed the barrier that
+        // ended that piece's tiles.
+        if (a.q_bulk) {
+            const int qs = cpiece & 1;
+            mbar_wait_bounded(qfull + 8 * qs, (cpiece >> 1) & 1, abort_flag, a.err, a.dbg, 5,
+                              cpiece);
+            const float* qr = qraw_s + qs * GS * HD;
+            const float2* cs = rope_s + qs * (HD / 2);
+            for (int idx = ctid; idx < GS * HD; idx += kConsumerThreads) {
+                const int g = idx / HD, d = idx % HD;
+                q_s[idx] = g < a.G ? rope_elem(qr + g * HD, d, pr.rope_half, cs, a.neox != 0) : 0.0f;
+            }
+            named_bar_sync(1, kConsumerThreads);
+            if (ctid == 0) mbar_arrive(qempty + 8 * qs);
+        } else {
         named_bar_sync(1, kConsumerThreads);
         if (JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
                               pr.rope_row < a.n_rope_rows && (kvh + 1) * a.G <= a.n_heads,
@@ -659,6 +816,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         named_bar_sync(1, kConsumerThreads);
+        }
+        ++cpiece;
+        if (pending_seg >= 0) {
+            // Every consumer thread's partial stores of the previous piece precede
+            // the barrier just passed, so this release publishes them; only
+            // warp 0 waits for it.
+            if (ctid == 0 && JX_CHECKED(a, pending_seg < a.n_segments, 63, pending_seg, 0, 0))
+                early_prev = atomic_add_release_gpu(a.counters + pending_seg, 1);
+            pending_seg = -1;
+        }
 
         float m[GS], l[GS], o[GS][G::DPL];
         if constexpr (kMma) {
@@ -868,7 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 O += o_s[(w * GS + g) * HD + d] * f;
             }
             if (whole) {
-                emit_final<HD>(a, pr, kvh * a.G + g, d, M, Lsum, O);
+                emit_final<HD>(a, pr.io, kvh * a.G + g, d, M, Lsum, O);
             } else if (JX_CHECKED(a, (slot + 1) * GS * (HD + 2) <= a.scratch_floats, 60, slot, seg, 0)) {
                 float* dst = a.scratch + (slot * GS + g) * (HD + 2);
                 dst[d] = O;
@@ -879,112 +1046,61 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         if (!whole) {
-            // Last CTA to finish this segment merges every piece (no waiting).
-            // Release: every writer reaches the barrier, then one thread fences
-            // and counts the piece in (the pattern of a grid-wide barrier).
-            named_bar_sync(1, kConsumerThreads);
-            const long long c_first = owner_cta(it.seg_start, a.total, P);
-            const long long c_last = owner_cta(it.seg_start + pr.len - 1, a.total, P);
-            if (ctid == 0 && !JX_CHECKED(a, seg >= 0 && seg < a.n_segments &&
-                                                c_last + seg < P + a.n_segments && c_first >= 0,
-                                         61, seg, c_first, c_last)) {
-                misc[0] = 0;
-            } else if (ctid == 0) {
-                const int prev = atomic_add_acq_rel_gpu(a.counters + seg, 1);
-                const bool last = prev == static_cast<int>(c_last - c_first);
-                if (last) a.counters[seg] = 0;  // every piece has arrived: ready for the next step
-                misc[0] = last ? 1 : 0;
+            // counted in after the CTA's last piece (at most the first and the
+            // last piece of a slice are not whole segments)
+            if (n_split < 2) {
+                const bool early = it.x < b1;  // more pieces follow in this CTA
+                if (ctid == 0) {
+                    SplitRec& r = recs[n_split];
+                    r.seg = seg;
+                    r.seg_start = it.seg_start;
+                    r.len = pr.len;
+                    r.io = pr.io;
+                    r.kvh = kvh;
+                    r.early = early ? 1 : 0;
+                }
+                if (early) pending_seg = seg;  // counted in after the next piece's first barrier
+                ++n_split;
+            } else {
+                (void)JX_CHECKED(a, false, 62, n_split, seg, 0);
             }
-            named_bar_sync(1, kConsumerThreads);
-            if (misc[0]) {
-                // (slots c_first+seg .. c_last+seg were bounds-checked above)
-                const int np = static_cast<int>(c_last - c_first + 1);
-                const int Gn = a.G;
-                float* ms = o_s;              // [np][G] piece maxima, then scale factors
-                float* ls = o_s + np * Gn;    // [np][G] piece sums
-                float* tot = ls + np * Gn;    // [G] merged max, [G] merged sum
-                const float* base_p = a.scratch + (c_first + seg) * GS * (HD + 2);
-                if ((2 * np + 2) * Gn <= kConsumerWarps * GS * HD) {
-                    // one parallel pass over every piece's (m, l) ...
-                    for (int idx = ctid; idx < np * Gn; idx += kConsumerThreads) {
-                        const int q = idx / Gn, g = idx % Gn;
-                        const float* src = base_p + (static_cast<long long>(q) * GS + g) * (HD + 2);
-                        ms[idx] = __ldcg(src + HD);
-                        ls[idx] = __ldcg(src + HD + 1);
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    // ... merged max, scale factors and sum per head ...
-                    for (int g = ctid; g < Gn; g += kConsumerThreads) {
-                        float M = -INFINITY;
-                        for (int q = 0; q < np; ++q) M = fmaxf(M, ms[q * Gn + g]);
-                        float Lsum = 0.0f;
-                        for (int q = 0; q < np; ++q) {
-                            const float mw = ms[q * Gn + g];
-                            const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
-                            ms[q * Gn + g] = f;
-                            Lsum += ls[q * Gn + g] * f;
-                        }
-                        tot[g] = M;
-                        tot[Gn + g] = Lsum;
-                    }
-                    named_bar_sync(1, kConsumerThreads);
-                    // ... then o: every load of a chunk of pieces is issued before any
-                    // is used (one round trip per chunk)
-                    constexpr int E = (GS * HD + kConsumerThreads - 1) / kConsumerThreads;
-                    constexpr int QC = (32 / E) < 1 ? 1 : ((32 / E) > 8 ? 8 : (32 / E));
-                    const long long step = static_cast<long long>(GS) * (HD + 2);
-                    float O[E];
-#pragma unroll
-                    for (int e = 0; e < E; ++e) O[e] = 0.0f;
-                    for (int q0 = 0; q0 < np; q0 += QC) {
-                        float vals[E][QC];
-#pragma unroll
-                        for (int e = 0; e < E; ++e) {
-                            const int idx = ctid + e * kConsumerThreads;
-                            const int g = idx / HD, d = idx % HD;
-                            const float* src = base_p + static_cast<long long>(g) * (HD + 2) + d;
-#pragma unroll
-                            for (int qq = 0; qq < QC; ++qq)
-                                vals[e][qq] = (idx < Gn * HD && q0 + qq < np)
-                                                  ? __ldcg(src + (q0 + qq) * step) : 0.0f;
-                        }
-#pragma unroll
-                        for (int e = 0; e < E; ++e) {
-                            const int idx = ctid + e * kConsumerThreads;
-                            const int g = idx / HD;
-#pragma unroll
-                            for (int qq = 0; qq < QC; ++qq)
-                                if (idx < Gn * HD && q0 + qq < np)
-                                    O[e] += vals[e][qq] * ms[(q0 + qq) * Gn + g];
-                        }
-                    }
-#pragma unroll
-                    for (int e = 0; e < E; ++e) {
-                        const int idx = ctid + e * kConsumerThreads;
-                        if (idx < Gn * HD) {
-                            const int g = idx / HD, d = idx % HD;
-                            emit_final<HD>(a, pr, kvh * Gn + g, d, tot[g], tot[Gn + g], O[e]);
-                        }
-                    }
-                } else {
-                    // more pieces than the staging area holds: merge directly
-                    for (int idx = ctid; idx < Gn * HD; idx += kConsumerThreads) {
-                        const int g = idx / HD, d = idx % HD;
-                        float M = -INFINITY;
-                        for (long long cc = c_first; cc <= c_last; ++cc)
-                            M = fmaxf(M, __ldcg(a.scratch + ((cc + seg) * GS + g) * (HD + 2) + HD));
-                        float Lsum = 0.0f, O = 0.0f;
-                        for (long long cc = c_first; cc <= c_last; ++cc) {
-                            const float* src = a.scratch + ((cc + seg) * GS + g) * (HD + 2);
-                            const float mw = __ldcg(src + HD);
-                            const float f = mw == -INFINITY ? 0.0f : ex2_approx((mw - M) * kLog2e);
-                            Lsum += __ldcg(src + HD + 1) * f;
-                            O += __ldcg(src + d) * f;
-                        }
-                        emit_final<HD>(a, pr, kvh * Gn + g, d, M, Lsum, O);
+        }
+    }
+    if (n_split > 0) {
+        // Release: every writer of a partial reaches the barrier, then one
+        // thread counts the CTA's last piece in with an acquire-release atomic
+        // (the pattern of a grid-wide barrier); an early count-in that turned
+        // out last gets an acquire fence.  The last CTA of a segment merges it.
+        named_bar_sync(1, kConsumerThreads);
+        if (ctid == 0) {
+            bool fence = false;
+            for (int k = 0; k < n_split; ++k) {
+                const SplitRec& r = recs[k];
+                const long long c_first = owner_cta(r.seg_start, a.total, P);
+                const long long c_last = owner_cta(r.seg_start + r.len - 1, a.total, P);
+                int last = 0;
+                if (JX_CHECKED(a, r.seg >= 0 && r.seg < a.n_segments &&
+                                      c_last + r.seg < P + a.n_segments && c_first >= 0 &&
+                                      (c_last + r.seg + 1) * GS * (HD + 2) <= a.scratch_floats,
+                               61, r.seg, c_first, c_last)) {
+                    const int prev =
+                        r.early ? early_prev : atomic_add_acq_rel_gpu(a.counters + r.seg, 1);
+                    last = prev == static_cast<int>(c_last - c_first) ? 1 : 0;
+                    if (last) {
+                        a.counters[r.seg] = 0;  // every piece arrived: ready for the next step
+                        fence = fence || r.early;
                     }
                 }
+                misc[2 + k] = last;
             }
+            if (fence) fence_acq_rel_gpu();
+        }
+        named_bar_sync(1, kConsumerThreads);
+        for (int k = 0; k < n_split; ++k) {
+            if (!misc[2 + k]) continue;  // the same for every consumer thread
+            const SplitRec r = recs[k];
+            merge_split<HD, GS>(a, r, owner_cta(r.seg_start, a.total, P),
+                                owner_cta(r.seg_start + r.len - 1, a.total, P), ctid);
         }
     }
     (void)JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);

@@ -17,11 +17,20 @@ template <int HD, int GP, int KP>
 struct Entry {
     static constexpr int DT = JX_INST_DT;
     static int smem(int stages) { return SmemLayout<HD, GP, DT, KP>::total(stages); }
+    // Kernel attributes: the dynamic shared memory it asks for, and the largest
+    // shared-memory carveout so that two CTAs of ~80-110 KB fit on one SM
+    // (the default carveout choice can leave room for only one).
+    static cudaError_t set_attributes(int bytes) {
+        cudaError_t e = cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+        return cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
+                                    cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cudaSharedmemCarveoutMaxShared);
+    }
     static int occupancy(int stages) {
         const int bytes = smem(stages);
-        if (cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
-            return 0;
+        if (set_attributes(bytes) != cudaSuccess) return 0;
         int n = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_kernel<HD, GP, DT, KP>, kThreads,
                                                           bytes) != cudaSuccess)
@@ -36,8 +45,7 @@ struct Entry {
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= 64 || set_bytes[dev] < bytes) {
-            e = cudaFuncSetAttribute(decode_kernel<HD, GP, DT, KP>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+            e = set_attributes(bytes);
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) set_bytes[dev] = bytes;
         }

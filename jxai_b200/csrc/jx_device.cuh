@@ -147,6 +147,18 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Untiled bulk copy global -> this CTA's shared memory (no multicast),
+// completion counted on an mbarrier.  Both addresses 16-byte aligned, `bytes`
+// a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -170,6 +182,20 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
     int old;
     asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
+}
+
+// Atomic add with release semantics at GPU scope: publishes the writes the
+// CTA made before a preceding barrier without waiting for other CTAs' writes.
+__device__ __forceinline__ int atomic_add_release_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.release.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// Acquire-release fence at GPU scope (after reading a counter that earlier
+// writers released, before reading their data).
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 // Named barrier over `count` threads (count a multiple of 32).

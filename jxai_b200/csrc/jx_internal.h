@@ -67,6 +67,8 @@ struct DecodeArgs {
     int n_cache_seqs;
     int smem_bytes;          // dynamic shared memory of the launch
     int* dbg;                // [8]: first failed check (code, block, values)
+    int q_bulk;              // 1: q rows and the rope table allow 16-byte bulk copies
+                             // (the producer prefetches each piece's q into shared memory)
 };
 
 // Host-side launch request for one fused decode launch.

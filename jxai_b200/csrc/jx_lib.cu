@@ -129,17 +129,20 @@ int consumers_for(int stages, int split) {
 }
 
 // Default pipeline depth / residency for one kernel configuration: a ring of
-// 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if it
-// fits, else with one CTA per SM, else the deepest ring that fits one CTA.
+// 8 or 4 stages (all four consumer warps busy) with two CTAs per SM if shared
+// memory and registers allow it, else with one CTA per SM, else the deepest
+// ring that fits one CTA.
 void default_shape(int hd, int gp, int kp, int dtype, int* stages, int* cps) {
     const int per_sm = 227 * 1024;
     for (int c = 2; c >= 1; --c)
-        for (int ns : {8, 4})
-            if (decode_smem_bytes(hd, gp, kp, dtype, ns) + 1024 * (c - 1) <= per_sm / c) {
-                *stages = ns;
-                *cps = c;
-                return;
-            }
+        for (int ns : {8, 4}) {
+            const int bytes = decode_smem_bytes(hd, gp, kp, dtype, ns);
+            if (bytes < 0 || bytes + 1024 * (c - 1) > per_sm / c) continue;
+            if (decode_ctas_per_sm(hd, gp, kp, dtype, ns) < c) continue;
+            *stages = ns;
+            *cps = c;
+            return;
+        }
     int best = 2;
     for (int ns = 7; ns >= 2; --ns)
         if (decode_smem_bytes(hd, gp, kp, dtype, ns) <= per_sm) { best = ns; break; }
@@ -669,6 +672,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.err = kv->d_err;
         A.n_stages = stages;
         A.n_consumers = consumers_for(stages, kp);
+        A.q_bulk = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;
         A.scratch_floats = static_cast<long long>(kv->scratch_floats);
