@@ -50,6 +50,8 @@ def parse_args():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--clock-probe-s", type=float, default=1.0,
                    help="untimed seconds of steps before warm-up so clocks leave idle")
+    p.add_argument("--seqs", type=int, default=0,
+                   help="keep only the first N sequences of the workload (small profiling cases)")
     p.add_argument("--no-graph", action="store_true",
                    help="time K eager launches instead of one CUDA graph of K launches")
     return p.parse_args()
@@ -235,6 +237,8 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
     torch.cuda.set_device(local_rank)
     w = W.make(args.config, args.dtype)
+    if args.seqs > 0:
+        w.lengths = w.lengths[:args.seqs]
     r = Runner(w, rank, world, local_rank)
     stream = torch.cuda.current_stream()
 
@@ -298,14 +302,16 @@ def run_ours(args, rank, world, local_rank):
         with torch.cuda.graph(graph, stream=gstream):
             for _ in range(K):
                 r.kernel()
-        graph.replay()  # untimed: uploads the graph
+        with torch.cuda.stream(gstream):
+            graph.replay()  # untimed: uploads the graph
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
         t_wall0 = time.time()
-        e_start.record(gstream)
-        graph.replay()
-        e_stop.record(gstream)
+        with torch.cuda.stream(gstream):  # replay() launches on the current stream
+            e_start.record(gstream)
+            graph.replay()
+            e_stop.record(gstream)
         torch.cuda.synchronize()
         t_wall1 = time.time()
         barrier()
@@ -483,6 +489,8 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     w = W.make(args.config, args.dtype)
+    if args.seqs > 0:
+        w.lengths = w.lengths[:args.seqs]
     orc, kind = _cpu_oracle()
     n_seqs, n_layers, kv_bytes = _cpu_sample_shape(w)
     rng = np.random.default_rng(W.SEED)
