@@ -43,7 +43,9 @@ enum {
     JX_ERR_NOMEM = -3,       /* device or pinned-host allocation failed */
     JX_ERR_UNSUPPORTED = -4, /* shape outside the compiled kernel set */
     JX_ERR_RANGE = -5,       /* position outside the cache (caller must compact first) */
-    JX_ERR_DEVICE = -6       /* a kernel reported a device-side error (bounded wait ran out) */
+    JX_ERR_DEVICE = -6,      /* a kernel reported a device-side error (bounded wait ran out) */
+    JX_ERR_TIMEOUT = -7,     /* a sharded step did not complete in time; communicator aborted */
+    JX_ERR_COMM = -8         /* an NCCL call failed or NCCL is not available */
 };
 
 /* KV element type.  JX_F16_TRUNC is jxai's native cache: fp16 written with the
@@ -160,6 +162,27 @@ JX_API int jx_attn_step_partial(jx_kv* kv, const jx_layer_desc* layers, uint32_t
 JX_API int jx_lse_merge(const float* gathered, uint32_t n_shards, uint64_t shard_stride,
                  uint32_t n_groups, uint32_t n_heads, uint32_t head_dim, float* out,
                  uint32_t out_stride, void* stream);
+
+/* The whole sequence-sharded step over NCCL: jx_attn_step_partial on this
+ * rank's shard (the positions [desc.pos_base, desc.pos_base + capacity) of the
+ * handle), one ncclAllGather of every rank's partials over `nccl_comm` (an
+ * ncclComm_t of all ranks, rank order = shard order), and the log-sum-exp
+ * merge into args->out (row stride args->q_stride) -- every rank receives the
+ * full output.  All layers of the call share head_dim.  Partial and gather
+ * buffers belong to the handle.  NCCL is the process's libnccl.so.2, found at
+ * run time (JX_ERR_COMM when absent).
+ * timeout_ms = 0: asynchronous on `stream`, like jx_attn_step.  timeout_ms > 0:
+ * the call also waits for the step to complete, polling NCCL's asynchronous
+ * error; if it has not completed within timeout_ms (a rank that never joins)
+ * it returns JX_ERR_TIMEOUT, on an NCCL error JX_ERR_COMM.  The work stays
+ * queued and the communicator untouched: aborting it is the caller's
+ * decision (ncclCommAbort).  (Callers with their own
+ * collectives can still compose jx_attn_step_partial, an all-gather and
+ * jx_lse_merge.)  The reference has no multi-GPU path: this extends
+ * transformer.cpp:2497-2567 to one context sharded by position. */
+JX_API int jx_attn_step_sharded(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                                const jx_step_args* args, void* nccl_comm, uint32_t timeout_ms,
+                                void* stream);
 
 /* The same step as jx_attn_step for callers that cannot allocate GPU memory.
  * No counterpart in the reference (its cache lives in host vectors).  For an

@@ -18,6 +18,8 @@ JX_ERR_NOMEM = -3
 JX_ERR_UNSUPPORTED = -4
 JX_ERR_RANGE = -5
 JX_ERR_DEVICE = -6
+JX_ERR_TIMEOUT = -7
+JX_ERR_COMM = -8
 
 JX_F32, JX_BF16, JX_F16_TRUNC = 0, 1, 2
 
@@ -28,7 +30,7 @@ EXPORTS = (
     "jx_kv_layer_ptr", "jx_attn_step", "jx_attn_step_partial", "jx_lse_merge",
     "jx_kv_check_device_error", "jx_kv_set_option", "jx_kv_last_launch_count",
     "jx_kv_fill_normal", "jx_fill_normal_f32", "jx_last_error_string", "jx_version",
-    "jx_attn_step_noalloc",
+    "jx_attn_step_noalloc", "jx_attn_step_sharded",
 )
 
 
@@ -87,6 +89,7 @@ def _declare(lib: C.CDLL) -> None:
         "jx_fill_normal_f32": [vp, u64, u64, u32, vp],
         "jx_attn_step_noalloc": [C.POINTER(KvDesc), vp, vp, C.POINTER(LayerDesc), u32,
                                  C.POINTER(StepArgs), vp],
+        "jx_attn_step_sharded": [vp, C.POINTER(LayerDesc), u32, C.POINTER(StepArgs), vp, u32, vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

@@ -301,6 +301,28 @@ def attn_step_partial(cache: KVCache, layers: Sequence[Layer], q, k, v, partials
                                          _stream_ptr(stream)))
 
 
+def attn_step_sharded(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos: Sequence[int],
+                      n_heads: int, n_kv_heads: int, comm, timeout_ms: int = 0,
+                      scale: Optional[float] = None, softcap: float = 0.0,
+                      sliding_window: int = 0, yarn_scale: float = 1.0, neox: bool = True,
+                      seq_ids: Optional[Sequence[int]] = None, stream=None) -> None:
+    """One context sharded by position over the ranks of an NCCL communicator.
+
+    This rank's cache holds positions [pos_base, pos_base + capacity); the call
+    runs the shard's partial step, all-gathers every rank's (o, m, l) over
+    `comm` (an ncclComm_t address, e.g. NcclComm.handle) and merges them into
+    `out` on every rank.  timeout_ms > 0 also waits for completion and raises
+    JxError code -7 when the step does not finish in time (the communicator
+    is left to the caller to abort).
+    """
+    arr, keep = _layer_array(layers)
+    a, keep2 = _step_args(cache, layers, q, k, v, out, pos, n_heads, n_kv_heads, scale, softcap,
+                          sliding_window, yarn_scale, neox, seq_ids, 0)
+    check(cache.lib.jx_attn_step_sharded(cache.handle, arr, len(layers), C.byref(a),
+                                         C.c_void_p(int(comm)), int(timeout_ms),
+                                         _stream_ptr(stream)))
+
+
 class StepPlan:
     """One attn_step (or attn_step_partial) call with its C arguments built once.
 

@@ -4,6 +4,11 @@
 // flattened work plan, and launches the fused kernel (jx_decode.cuh), plus the
 // log-sum-exp merge of sequence shards and the seeded fill used by benches.
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>  // types and enum values only: the functions are resolved at run time
+
+#include <chrono>
+#include <thread>
 
 #include <algorithm>
 #include <cmath>
@@ -272,6 +277,10 @@ struct jx_kv {
     uint64_t replay_generation = ~0ull;
     std::vector<unsigned char> replay_key;
     std::vector<DecodeLaunch> replay;
+    // sequence-sharded step: this rank's partials and the gathered partials
+    float* d_part = nullptr;
+    float* d_gather = nullptr;
+    size_t part_floats = 0, gather_floats = 0;
 };
 
 namespace {
@@ -706,6 +715,92 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     return JX_OK;
 }
 
+// NCCL entry points used by the sharded step, taken from the process's
+// libnccl.so.2 (the copy a framework already loaded, else the system one), so
+// the library has no link-time NCCL dependency.
+struct NcclApi {
+    bool ok = false;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*comm_count)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*comm_user_rank)(const ncclComm_t, int*) = nullptr;
+    ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+    const char* (*get_error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl_api() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+        api.comm_count = reinterpret_cast<decltype(api.comm_count)>(dlsym(h, "ncclCommCount"));
+        api.comm_user_rank =
+            reinterpret_cast<decltype(api.comm_user_rank)>(dlsym(h, "ncclCommUserRank"));
+        api.comm_get_async_error = reinterpret_cast<decltype(api.comm_get_async_error)>(
+            dlsym(h, "ncclCommGetAsyncError"));
+        api.get_error_string =
+            reinterpret_cast<decltype(api.get_error_string)>(dlsym(h, "ncclGetErrorString"));
+        api.ok = api.all_gather && api.comm_count && api.comm_user_rank &&
+                 api.comm_get_async_error && api.get_error_string;
+    });
+    return api;
+}
+
+int grow(float** p, size_t* have, size_t need) {
+    if (*have >= need) return JX_OK;
+    if (*p) JX_CUDA(cudaFree(*p));
+    *p = nullptr;
+    *have = 0;
+    if (cudaMalloc(p, need * sizeof(float)) != cudaSuccess)
+        return fail(JX_ERR_NOMEM, "allocation of %zu floats failed", need);
+    *have = need;
+    return JX_OK;
+}
+
+// Waits for `stream` to reach the point of the call, polling NCCL's
+// asynchronous error.  It never aborts the communicator itself: whether to
+// abort (and how the process recovers) stays with the caller.
+int wait_sharded(const NcclApi& nc, ncclComm_t comm, cudaStream_t stream, uint32_t timeout_ms) {
+    cudaEvent_t ev = nullptr;
+    JX_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    cudaError_t e = cudaEventRecord(ev, stream);
+    if (e != cudaSuccess) {
+        cudaEventDestroy(ev);
+        return fail(JX_ERR_CUDA, "cudaEventRecord: %s", cudaGetErrorString(e));
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    int rc = JX_OK;
+    for (;;) {
+        e = cudaEventQuery(ev);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) {
+            rc = fail(JX_ERR_CUDA, "sharded step: %s", cudaGetErrorString(e));
+            break;
+        }
+        ncclResult_t ae = ncclSuccess;
+        if (nc.comm_get_async_error(comm, &ae) == ncclSuccess && ae != ncclSuccess &&
+            ae != ncclInProgress) {
+            rc = fail(JX_ERR_COMM, "NCCL asynchronous error: %s", nc.get_error_string(ae));
+            break;
+        }
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                            std::chrono::steady_clock::now() - t0)
+                            .count();
+        if (ms > static_cast<long long>(timeout_ms)) {
+            rc = fail(JX_ERR_TIMEOUT,
+                      "sharded step did not complete within %u ms (a rank did not join?)",
+                      timeout_ms);
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    cudaEventDestroy(ev);
+    return rc;
+}
+
 }  // namespace
 
 // ================================================================== C ABI
@@ -778,6 +873,8 @@ int jx_kv_destroy(jx_kv* kv) {
     cudaFree(kv->d_rows);
     cudaFree(kv->d_scratch);
     cudaFree(kv->d_counters);
+    cudaFree(kv->d_part);
+    cudaFree(kv->d_gather);
     for (PlanSlot& s : kv->slots) {
         if (s.ev) cudaEventDestroy(s.ev);
         cudaFree(s.d_buf);
@@ -899,6 +996,46 @@ int jx_attn_step_partial(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_laye
                          const jx_step_args* args, float* partials, void* stream) {
     if (!partials) return fail(JX_ERR_INVALID, "null partials");
     return step_impl(kv, layers, n_layers, args, partials, (cudaStream_t)stream);
+}
+
+int jx_attn_step_sharded(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                         const jx_step_args* args, void* nccl_comm, uint32_t timeout_ms,
+                         void* stream) {
+    if (!kv || !layers || !args || !nccl_comm || !args->out || n_layers == 0)
+        return fail(JX_ERR_INVALID, "null handle, layers, args, communicator or output");
+    const uint32_t hd = layers[0].head_dim;
+    for (uint32_t l = 1; l < n_layers; ++l)
+        if (layers[l].head_dim != hd)
+            return fail(JX_ERR_UNSUPPORTED, "all layers of a sharded step must share head_dim");
+    if (args->n_seqs == 0 || args->n_heads == 0 || hd == 0)
+        return fail(JX_ERR_INVALID, "empty step");
+    if (args->q_stride < static_cast<uint64_t>(args->n_heads) * hd)
+        return fail(JX_ERR_INVALID, "q_stride smaller than n_heads*head_dim");
+    const NcclApi& nc = nccl_api();
+    if (!nc.ok) return fail(JX_ERR_COMM, "NCCL (libnccl.so.2) is not available in this process");
+    ncclComm_t comm = static_cast<ncclComm_t>(nccl_comm);
+    int world = 0, rank = -1;
+    if (nc.comm_count(comm, &world) != ncclSuccess || nc.comm_user_rank(comm, &rank) != ncclSuccess ||
+        world <= 0 || rank < 0 || rank >= world)
+        return fail(JX_ERR_COMM, "cannot query the communicator's size and rank");
+    const uint64_t groups = static_cast<uint64_t>(args->n_seqs) * n_layers;
+    const size_t per = static_cast<size_t>(groups * args->n_heads * (hd + 2));
+    DeviceGuard guard(kv->d.device);
+    if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
+    int rc = grow(&kv->d_part, &kv->part_floats, per);
+    if (!rc) rc = grow(&kv->d_gather, &kv->gather_floats, per * static_cast<size_t>(world));
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = jx_attn_step_partial(kv, layers, n_layers, args, kv->d_part, stream);
+    if (rc) return rc;
+    const ncclResult_t r = nc.all_gather(kv->d_part, kv->d_gather, per, ncclFloat32, comm, st);
+    if (r != ncclSuccess)
+        return fail(JX_ERR_COMM, "ncclAllGather: %s", nc.get_error_string(r));
+    rc = jx_lse_merge(kv->d_gather, static_cast<uint32_t>(world), per, static_cast<uint32_t>(groups),
+                      args->n_heads, hd, args->out, static_cast<uint32_t>(args->q_stride), stream);
+    if (rc) return rc;
+    if (timeout_ms > 0) return wait_sharded(nc, comm, st, timeout_ms);
+    return JX_OK;
 }
 
 int jx_lse_merge(const float* gathered, uint32_t n_shards, uint64_t shard_stride,

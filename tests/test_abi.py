@@ -73,6 +73,8 @@ def test_invalid_arguments_rejected_on_host():
     assert b"null" in lib.jx_last_error_string()
     assert lib.jx_attn_step(None, None, 0, None, None) == _lib.JX_ERR_INVALID
     assert lib.jx_lse_merge(None, 0, 0, 0, 0, 0, None, 0, None) == _lib.JX_ERR_INVALID
+    assert lib.jx_attn_step_sharded(None, None, 0, None, None, 0, None) == _lib.JX_ERR_INVALID
+    assert b"communicator" in lib.jx_last_error_string()
 
 
 def test_no_gpu_means_a_loud_failure():
