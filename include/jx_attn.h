@@ -208,8 +208,12 @@ JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache, void* v_c
  * *code = 0 when no kernel reported an error. */
 JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
 
-/* Launch-shape overrides for tuning sweeps: key "ctas_per_sm" or "stages";
- * value 0 restores the default. */
+/* Launch options: "ctas_per_sm", "stages" and "grid" override the launch shape
+ * (tuning sweeps; 0 restores the default); "pdl" 1 / 0 / -1 (default: on
+ * for steps of at least 2^17 attended rows) turns programmatic dependent
+ * launch of the decode kernel on / off / automatic (with it, a step's launch
+ * and set-up overlap the previous kernel's tail; its data accesses still wait
+ * for that kernel to complete). */
 JX_API int jx_kv_set_option(jx_kv* kv, const char* key, int value);
 
 /* Number of kernels the last jx_attn_step / jx_attn_step_partial launched. */

@@ -599,6 +599,9 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // The next step may be scheduled onto SMs as this grid frees them; it
+    // waits (pdl_wait) for this grid's completion before touching any data.
+    pdl_launch_dependents();
     if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) +
                                8 * (2 * NS + L::n_extra_bars) <= a.smem_bytes &&
                            a.n_consumers >= kSplit && a.n_consumers <= kConsumerWarps &&
@@ -640,6 +643,9 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         int n_issued = 0;  // tiles [0, n_issued) had their loads issued
         int piece = 0;
         while (it.next()) {
+            // the work plan was read above; everything below may touch data an
+            // earlier kernel of the stream wrote (q/k/v inputs, cache rows)
+            if (piece == 0) pdl_wait();
             const PairRow& pr = it.pr;
             const int ntiles = (it.n + kTileRows - 1) / kTileRows;
             if (!JX_CHECKED(a, it.kvh >= 0 && it.kvh < a.n_kv && pr.cache_layer >= 0 &&
@@ -747,6 +753,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
 
     // ---------------------------------------------------------------- consumers
     const int ctid = threadIdx.x;
+    pdl_wait();  // outputs, partials and counters were last written by an earlier step
 
     // Partial mode: pairs with no local rows still owe an (o=0, m=-inf, l=0) partial.
     if (a.part_out) {

@@ -49,8 +49,17 @@ struct Entry {
             if (e != cudaSuccess) return e;
             if (dev >= 0 && dev < 64) set_bytes[dev] = bytes;
         }
-        decode_kernel<HD, GP, DT, KP><<<L.grid, kThreads, bytes, L.stream>>>(*L.tmK, *L.tmV, L.args);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(L.grid));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = static_cast<size_t>(bytes);
+        cfg.stream = L.stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = L.pdl ? 1 : 0;
+        return cudaLaunchKernelEx(&cfg, decode_kernel<HD, GP, DT, KP>, *L.tmK, *L.tmV, L.args);
     }
 };
 

@@ -198,6 +198,16 @@ __device__ __forceinline__ void fence_acq_rel_gpu() {
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel of
+// the stream (launched with programmatic stream serialisation) be scheduled
+// onto SMs this grid frees; wait blocks until every prerequisite grid has
+// completed and its memory is visible -- nothing a previous kernel may have
+// written is read or written before it.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier over `count` threads (count a multiple of 32).
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");

@@ -82,6 +82,7 @@ struct DecodeLaunch {
     int dtype;   // 0 f32, 1 bf16, 2 f16 trunc
     int grid;
     int stages;
+    int pdl;     // launch with programmatic stream serialisation
     cudaStream_t stream;
 };
 
