@@ -213,8 +213,14 @@ JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
  * for steps of at least 2^17 attended rows) turns programmatic dependent
  * launch of the decode kernel on / off / automatic (with it, a step's launch
  * and set-up overlap the previous kernel's tail; its data accesses still wait
- * for that kernel to complete). */
+ * for that kernel to complete); "timing" 1 records events around every
+ * jx_attn_step / jx_attn_step_partial (not while a stream is being captured). */
 JX_API int jx_kv_set_option(jx_kv* kv, const char* key, int value);
+
+/* Device time of the last step recorded with option "timing" (waits for it):
+ * the counterpart of forward_token's attention_ms (transformer.cpp:2499, 2567),
+ * the wall time of RoPE + append + attention. */
+JX_API int jx_kv_last_step_ms(jx_kv* kv, float* ms);
 
 /* Number of kernels the last jx_attn_step / jx_attn_step_partial launched. */
 JX_API int jx_kv_last_launch_count(const jx_kv* kv, int* count);

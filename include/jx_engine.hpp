@@ -1,0 +1,219 @@
+// jx_engine.hpp -- C++ drop-in for jxai's KVCacheSlot and the attention block
+// of MoETransformerEngine::forward_token, over the C ABI of jx_attn.h.
+//
+// The reference keeps each slot's cache in host vectors (include/transformer.h:
+// 115-131) and runs RoPE, the KV append and grouped-query attention inline per
+// layer (src/transformer.cpp:2497-2567) on host q/k/v vectors.  Here the cache
+// lives in HBM (one jx_kv handle for all slots) and the block is one library
+// call per layer; the engine's surrounding code keeps its host vectors:
+//
+//   jx::DeviceKVCache cache(hp, max_slots);            // KVCacheSlot::init for all slots
+//   jx::KVCacheSlot& slot = ...; slot.init(id, cache);
+//   jx::AttentionBlock attn(cache);                     // device staging buffers
+//   // per layer, in place of transformer.cpp:2497-2567:
+//   attn.forward(slot, layer_desc, q.data(), k.data(), v.data(), attn_out.data(), pos);
+//   // after the last layer, as transformer.cpp:2792:
+//   slot.seq_pos++;
+//
+// Header-only; link with libjxattn.so and the CUDA runtime.  Every call
+// returns a jx status (0 = JX_OK); jx_last_error_string() has the message.
+#ifndef JX_ENGINE_HPP
+#define JX_ENGINE_HPP
+
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <vector>
+
+#include "jx_attn.h"
+
+namespace jx {
+
+// The attention-related fields of jxai's ModelHyperparams.
+struct Hyper {
+    uint32_t n_layers = 0;
+    uint32_t n_heads = 0;
+    uint32_t n_kv_heads = 0;
+    uint32_t q_dim = 0;              // max over layers (row stride of q / attn_out)
+    uint32_t kv_dim = 0;             // max over layers (row stride of the cache and k / v)
+    uint32_t kv_cache_capacity = 0;
+    uint32_t sliding_window = 0;
+    float yarn_scale = 1.0f;
+    float attn_logit_softcapping = 0.0f;
+    bool rope_neox = true;
+    bool unit_scale = false;         // gemma4: scale 1 instead of 1/sqrt(head_dim)
+};
+
+// The cache of every slot: KVCacheSlot::init's allocation for max_slots slots.
+class DeviceKVCache {
+  public:
+    DeviceKVCache(const Hyper& hp, uint32_t max_slots, jx_dtype dtype = JX_F16_TRUNC,
+                  int device = 0)
+        : hp_(hp) {
+        jx_kv_desc d{};
+        d.n_seqs = max_slots;
+        d.n_layers = hp.n_layers;
+        d.capacity = hp.kv_cache_capacity > 0 ? hp.kv_cache_capacity : 1;
+        d.row_stride = hp.kv_dim;
+        d.dtype = dtype;
+        d.device = device;
+        d.pos_base = 0;
+        status_ = jx_kv_create(&d, &kv_);
+    }
+    ~DeviceKVCache() { jx_kv_destroy(kv_); }
+    DeviceKVCache(const DeviceKVCache&) = delete;
+    DeviceKVCache& operator=(const DeviceKVCache&) = delete;
+
+    int status() const { return status_; }  // JX_OK when the allocation succeeded
+    jx_kv* handle() const { return kv_; }
+    const Hyper& hyper() const { return hp_; }
+
+  private:
+    Hyper hp_;
+    jx_kv* kv_ = nullptr;
+    int status_ = JX_ERR_INVALID;
+};
+
+// moe::KVCacheSlot with its cache on the device: the same members and methods
+// (transformer.cpp:13-66).  seq_pos is the engine's to advance, as in the
+// reference; the device copy of it is synchronised by every call below.
+struct KVCacheSlot {
+    uint32_t slot_id = 0;
+    uint32_t seq_pos = 0;
+    uint32_t compactions = 0;
+    std::vector<uint32_t> token_history;
+    DeviceKVCache* cache = nullptr;
+
+    int init(uint32_t id, DeviceKVCache& c) {
+        cache = &c;
+        slot_id = id;
+        compactions = 0;
+        token_history.clear();
+        return clear();
+    }
+    // zero rows, seq_pos 0 (transformer.cpp:25-30)
+    int clear(cudaStream_t stream = nullptr) {
+        seq_pos = 0;
+        token_history.clear();
+        return jx_kv_clear(cache->handle(), slot_id, stream);
+    }
+    // never moves forward (transformer.cpp:32-39)
+    int rollback(uint32_t new_seq_pos) {
+        if (new_seq_pos < seq_pos) seq_pos = new_seq_pos;
+        if (token_history.size() > new_seq_pos) token_history.resize(new_seq_pos);
+        return jx_kv_set_seq_pos(cache->handle(), slot_id, seq_pos);
+    }
+    // 4 sink rows + the last keep_recent rows (transformer.cpp:41-66)
+    int compact(uint32_t keep_recent = 128, cudaStream_t stream = nullptr) {
+        int rc = jx_kv_set_seq_pos(cache->handle(), slot_id, seq_pos);
+        if (rc) return rc;
+        const uint32_t before = seq_pos;
+        rc = jx_kv_compact(cache->handle(), slot_id, keep_recent, stream);
+        if (rc) return rc;
+        uint32_t after = before;
+        rc = jx_kv_get_seq_pos(cache->handle(), slot_id, &after);
+        if (rc) return rc;
+        if (after != before) {
+            seq_pos = after;
+            if (token_history.size() > after) token_history.resize(after);
+            compactions++;
+        }
+        return JX_OK;
+    }
+};
+
+// The per-layer attention fields of jxai's LayerDenseWeights.
+struct LayerAttn {
+    uint32_t head_dim = 0;
+    uint32_t rope_dim = 0;
+    float rope_freq_base = 10000.0f;
+    uint32_t kv_source_layer = 0;
+    bool is_swa = false;
+    bool shares_kv = false;
+    const float* rope_freqs = nullptr;  // host, rope_dim/2 factors (Neox, global layers)
+};
+
+// transformer.cpp:2497-2567 for one layer of one slot, host vectors in and
+// out: q (n_heads*head_dim) and k, v (n_kv_heads*head_dim) go up, attn_out
+// (n_heads*head_dim) comes down.  As in the reference, q and k are the
+// un-rotated projections and the call rotates them; unlike the reference the
+// host q and k are left unrotated (nothing reads them afterwards).
+class AttentionBlock {
+  public:
+    explicit AttentionBlock(DeviceKVCache& c, cudaStream_t stream = nullptr)
+        : cache_(c), stream_(stream) {
+        const Hyper& hp = c.hyper();
+        status_ = JX_OK;
+        if (cudaMalloc(&d_q_, sizeof(float) * hp.q_dim) != cudaSuccess ||
+            cudaMalloc(&d_k_, sizeof(float) * hp.kv_dim) != cudaSuccess ||
+            cudaMalloc(&d_v_, sizeof(float) * hp.kv_dim) != cudaSuccess ||
+            cudaMalloc(&d_out_, sizeof(float) * hp.q_dim) != cudaSuccess)
+            status_ = JX_ERR_NOMEM;
+    }
+    ~AttentionBlock() {
+        cudaFree(d_q_);
+        cudaFree(d_k_);
+        cudaFree(d_v_);
+        cudaFree(d_out_);
+    }
+    AttentionBlock(const AttentionBlock&) = delete;
+    AttentionBlock& operator=(const AttentionBlock&) = delete;
+
+    int status() const { return status_; }
+
+    int forward(KVCacheSlot& slot, const LayerAttn& lw, const float* q, const float* k,
+                const float* v, float* attn_out, uint32_t pos) {
+        if (status_) return status_;
+        const Hyper& hp = cache_.hyper();
+        const size_t q_dim = static_cast<size_t>(hp.n_heads) * lw.head_dim;
+        const size_t kv_dim = static_cast<size_t>(hp.n_kv_heads) * lw.head_dim;
+        if (cudaMemcpyAsync(d_q_, q, q_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(d_k_, k, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(d_v_, v, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+            return JX_ERR_CUDA;
+        jx_layer_desc L{};
+        L.head_dim = lw.head_dim;
+        L.rope_dim = lw.rope_dim;
+        L.rope_freq_base = lw.rope_freq_base;
+        L.kv_source_layer = lw.kv_source_layer;
+        L.is_swa = lw.is_swa ? 1 : 0;
+        L.shares_kv = lw.shares_kv ? 1 : 0;
+        L.rope_freqs = lw.rope_freqs;
+        int32_t seq = static_cast<int32_t>(slot.slot_id), p = static_cast<int32_t>(pos);
+        jx_step_args a{};
+        a.n_heads = hp.n_heads;
+        a.n_kv_heads = hp.n_kv_heads;
+        a.n_seqs = 1;
+        a.seq_ids = &seq;
+        a.pos = &p;
+        a.q = d_q_;
+        a.k = d_k_;
+        a.v = d_v_;
+        a.out = d_out_;
+        a.q_stride = hp.q_dim;
+        a.kv_stride = hp.kv_dim;
+        a.scale = hp.unit_scale ? 1.0f : 1.0f / std::sqrt(static_cast<float>(lw.head_dim));
+        a.softcap = hp.attn_logit_softcapping;
+        a.sliding_window = hp.sliding_window;
+        a.yarn_scale = hp.yarn_scale;
+        a.rope_neox = hp.rope_neox ? 1 : 0;
+        int rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_);
+        if (rc) return rc;
+        if (cudaMemcpyAsync(attn_out, d_out_, q_dim * 4, cudaMemcpyDeviceToHost, stream_) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(stream_) != cudaSuccess)
+            return JX_ERR_CUDA;
+        return JX_OK;
+    }
+
+  private:
+    DeviceKVCache& cache_;
+    cudaStream_t stream_;
+    float *d_q_ = nullptr, *d_k_ = nullptr, *d_v_ = nullptr, *d_out_ = nullptr;
+    int status_ = JX_ERR_INVALID;
+};
+
+}  // namespace jx
+
+#endif  // JX_ENGINE_HPP

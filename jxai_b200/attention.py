@@ -172,6 +172,13 @@ class KVCache:
         check(self.lib.jx_kv_last_launch_count(self.handle, C.byref(n)))
         return n.value
 
+    def last_step_ms(self) -> float:
+        """Device time of the last step (needs set_option("timing", 1)); the
+        reference's attention_ms."""
+        ms = C.c_float()
+        check(self.lib.jx_kv_last_step_ms(self.handle, C.byref(ms)))
+        return ms.value
+
     def synchronize(self, stream=None) -> None:
         try:
             import torch

@@ -268,6 +268,9 @@ struct jx_kv {
     std::vector<PlanSlot> slots;
     int opt_ctas_per_sm = 0, opt_stages = 0, opt_grid = 0;
     int opt_pdl = -1;  // programmatic dependent launch: -1 auto, 0 off, 1 on
+    int opt_timing = 0;  // 1: events around every step (jx_kv_last_step_ms)
+    cudaEvent_t ev_t0 = nullptr, ev_t1 = nullptr;
+    bool timed = false;  // a timed step was recorded
     int last_launches = 0;
     // launch shape per (head_dim, group, stages override): {stages, ctas per SM}
     std::map<std::tuple<int, int, int, int>, std::pair<int, int>> shapes;
@@ -808,6 +811,28 @@ int wait_sharded(const NcclApi& nc, ncclComm_t comm, cudaStream_t stream, uint32
 
 }  // namespace
 
+namespace {
+
+// step_impl between two events when the handle's "timing" option is on: the
+// device time of everything the step queued (plan upload when it changed,
+// launches) -- the counterpart of forward_token's attention_ms
+// (transformer.cpp:2499, 2567).
+int timed_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
+               float* partials, cudaStream_t stream) {
+    if (!kv || !kv->opt_timing) return step_impl(kv, layers, n_layers, a, partials, stream);
+    DeviceGuard guard(kv->d.device);
+    if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
+    if (!kv->ev_t0) JX_CUDA(cudaEventCreate(&kv->ev_t0));
+    if (!kv->ev_t1) JX_CUDA(cudaEventCreate(&kv->ev_t1));
+    JX_CUDA(cudaEventRecord(kv->ev_t0, stream));
+    const int rc = step_impl(kv, layers, n_layers, a, partials, stream);
+    JX_CUDA(cudaEventRecord(kv->ev_t1, stream));
+    kv->timed = rc == JX_OK;
+    return rc;
+}
+
+}  // namespace
+
 // ================================================================== C ABI
 
 extern "C" {
@@ -880,6 +905,8 @@ int jx_kv_destroy(jx_kv* kv) {
     cudaFree(kv->d_counters);
     cudaFree(kv->d_part);
     cudaFree(kv->d_gather);
+    if (kv->ev_t0) cudaEventDestroy(kv->ev_t0);
+    if (kv->ev_t1) cudaEventDestroy(kv->ev_t1);
     for (PlanSlot& s : kv->slots) {
         if (s.ev) cudaEventDestroy(s.ev);
         cudaFree(s.d_buf);
@@ -994,13 +1021,22 @@ int jx_kv_layer_ptr(jx_kv* kv, uint32_t seq, uint32_t layer, int which, void** p
 
 int jx_attn_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
                  const jx_step_args* args, void* stream) {
-    return step_impl(kv, layers, n_layers, args, nullptr, (cudaStream_t)stream);
+    return timed_step(kv, layers, n_layers, args, nullptr, (cudaStream_t)stream);
 }
 
 int jx_attn_step_partial(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
                          const jx_step_args* args, float* partials, void* stream) {
     if (!partials) return fail(JX_ERR_INVALID, "null partials");
-    return step_impl(kv, layers, n_layers, args, partials, (cudaStream_t)stream);
+    return timed_step(kv, layers, n_layers, args, partials, (cudaStream_t)stream);
+}
+
+int jx_kv_last_step_ms(jx_kv* kv, float* ms) {
+    if (!kv || !ms) return fail(JX_ERR_INVALID, "null argument");
+    if (!kv->timed) return fail(JX_ERR_INVALID, "no timed step (set option \"timing\" to 1)");
+    DeviceGuard guard(kv->d.device);
+    JX_CUDA(cudaEventSynchronize(kv->ev_t1));
+    JX_CUDA(cudaEventElapsedTime(ms, kv->ev_t0, kv->ev_t1));
+    return JX_OK;
 }
 
 int jx_attn_step_sharded(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
@@ -1097,6 +1133,7 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
         kv->opt_stages = value;
     } else if (!std::strcmp(key, "grid")) kv->opt_grid = value;
     else if (!std::strcmp(key, "pdl")) kv->opt_pdl = value < 0 ? -1 : (value ? 1 : 0);
+    else if (!std::strcmp(key, "timing")) kv->opt_timing = value ? 1 : 0;
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;
 }

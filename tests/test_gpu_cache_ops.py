@@ -177,3 +177,20 @@ def test_unsharded_step_refuses_positions_outside_the_cache():
         jx.attn_step(jx.KVCache(1, 1, 16, 128, "f32"), layers, q, k, k, q.clone(), [16], 4, 2)
     assert e.value.code == -5
     cache.close()
+
+
+def test_step_timer_reports_device_time():
+    # the counterpart of forward_token's attention_ms (transformer.cpp:2499, 2567)
+    import jxai_b200 as jx
+    torch = _torch()
+    cache = jx.KVCache(1, 2, 512, 128, "f32")
+    layers = [jx.Layer(64, 64, 1e4, 0), jx.Layer(64, 64, 1e4, 1)]
+    q = torch.zeros(1, 2, 4 * 64, device="cuda")
+    k = torch.zeros(1, 2, 128, device="cuda")
+    with pytest.raises(jx.JxError):
+        cache.last_step_ms()           # nothing timed yet
+    cache.set_option("timing", 1)
+    jx.attn_step(cache, layers, q, k, k, q.clone(), [300], 4, 2)
+    ms = cache.last_step_ms()
+    assert 0.0 < ms < 1000.0
+    cache.close()
