@@ -146,6 +146,19 @@ JX_API int jx_kv_layer_ptr(jx_kv* kv, uint32_t seq, uint32_t layer, int which, v
 JX_API int jx_attn_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
                  const jx_step_args* args, void* stream);
 
+/* Multi-token prefill: many tokens per call (the reference feeds a prompt
+ * token by token through forward_token, transformer.cpp:3092-3095).  Rows of
+ * `args` are tokens: args->seq_ids[i] (may repeat; NULL = all sequence 0) and
+ * args->pos[i], each (sequence, position) once; q/k/v/out are
+ * [n_rows][n_layers][stride] as in a step.  Every row's k and v are rotated
+ * and appended first (one launch), then every row attends over its
+ * sequence's rows up to its own position (window rules as in a step) --
+ * causal attention, the result of running the rows through jx_attn_step one
+ * position at a time.  Each row reads its own attended rows (no reuse of a
+ * K/V tile across query rows). */
+JX_API int jx_attn_prefill(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                           const jx_step_args* args, void* stream);
+
 /* Sequence-sharded variant for one long context split across GPUs: the same
  * step over this shard's rows only, writing per (sequence, layer, head) the
  * unnormalised partial [o[0..head_dim), m, l] (head_dim+2 floats, row-major

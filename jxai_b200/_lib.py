@@ -30,7 +30,7 @@ EXPORTS = (
     "jx_kv_layer_ptr", "jx_attn_step", "jx_attn_step_partial", "jx_lse_merge",
     "jx_kv_check_device_error", "jx_kv_set_option", "jx_kv_last_launch_count",
     "jx_kv_fill_normal", "jx_fill_normal_f32", "jx_last_error_string", "jx_version",
-    "jx_attn_step_noalloc", "jx_attn_step_sharded", "jx_kv_last_step_ms",
+    "jx_attn_step_noalloc", "jx_attn_step_sharded", "jx_kv_last_step_ms", "jx_attn_prefill",
 )
 
 
@@ -91,6 +91,7 @@ def _declare(lib: C.CDLL) -> None:
                                  C.POINTER(StepArgs), vp],
         "jx_attn_step_sharded": [vp, C.POINTER(LayerDesc), u32, C.POINTER(StepArgs), vp, u32, vp],
         "jx_kv_last_step_ms": [vp, C.POINTER(C.c_float)],
+        "jx_attn_prefill": [vp, C.POINTER(LayerDesc), u32, C.POINTER(StepArgs), vp],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

@@ -292,6 +292,22 @@ def attn_step(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos: Sequen
     check(cache.lib.jx_attn_step(cache.handle, arr, len(layers), C.byref(a), _stream_ptr(stream)))
 
 
+def attn_prefill(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos: Sequence[int],
+                 n_heads: int, n_kv_heads: int, seq_ids: Optional[Sequence[int]] = None,
+                 scale: Optional[float] = None, softcap: float = 0.0, sliding_window: int = 0,
+                 yarn_scale: float = 1.0, neox: bool = True, stream=None) -> None:
+    """Many tokens per call: row i is a token of sequence seq_ids[i] (default 0)
+    at position pos[i]; all rows are appended, then each attends causally.
+    q/out: [n_rows, n_layers, q_stride]; k/v: [n_rows, n_layers, kv_stride]."""
+    if seq_ids is None:
+        seq_ids = [0] * len(pos)
+    arr, keep = _layer_array(layers)
+    a, keep2 = _step_args(cache, layers, q, k, v, out, pos, n_heads, n_kv_heads, scale, softcap,
+                          sliding_window, yarn_scale, neox, seq_ids, 0)
+    check(cache.lib.jx_attn_prefill(cache.handle, arr, len(layers), C.byref(a),
+                                    _stream_ptr(stream)))
+
+
 def attn_step_partial(cache: KVCache, layers: Sequence[Layer], q, k, v, partials,
                       pos: Sequence[int], n_heads: int, n_kv_heads: int,
                       scale: Optional[float] = None, softcap: float = 0.0,

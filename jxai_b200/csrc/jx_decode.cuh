@@ -686,7 +686,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             // the tile; later pieces find the ring full of the previous piece, so
             // their append goes first and its latency hides behind those tiles.
             int t_app = -1;
-            if (pr.append_row >= 0) {
+            if (pr.append_row >= 0 && !a.skip_append) {
                 const int al = pr.append_row - pr.row0;
                 if (al >= it.r && al < it.r + it.n) t_app = (al - it.r) / kTileRows;
             }

@@ -69,6 +69,7 @@ struct DecodeArgs {
     int* dbg;                // [8]: first failed check (code, block, values)
     int q_bulk;              // 1: q rows and the rope table allow 16-byte bulk copies
                              // (the producer prefetches each piece's q into shared memory)
+    int skip_append;         // 1: rows were appended by an earlier launch (prefill)
 };
 
 // Host-side launch request for one fused decode launch.

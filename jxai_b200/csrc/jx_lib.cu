@@ -124,6 +124,33 @@ __global__ void fill_f32_kernel(float* dst, uint64_t n, uint64_t seed, uint32_t 
         dst[i] = normal_at(seed, stream_id, i);
 }
 
+// Multi-token prefill, first pass: every pair's k row rotated and k, v stored
+// at its position (the append of transformer.cpp:2506-2520 for all tokens of
+// the call) before any of them attends.  One block per pair.
+template <int DT>
+__global__ void append_rows_kernel(const PairRow* __restrict__ pairs, int n_pairs,
+                                   const float2* __restrict__ rope, int rope_width,
+                                   const float* __restrict__ k_in, const float* __restrict__ v_in,
+                                   long long kv_stride, int n_kv, int hd, int neox, void* kc,
+                                   void* vc, long long seq_stride, long long layer_stride,
+                                   long long row_stride) {
+    const int i = blockIdx.x;
+    if (i >= n_pairs) return;
+    const PairRow pr = pairs[i];
+    if (pr.append_row < 0) return;
+    const float2* cs = rope + static_cast<long long>(pr.rope_row) * rope_width;
+    const long long dst0 = static_cast<long long>(pr.seq) * seq_stride +
+                           static_cast<long long>(pr.cache_layer) * layer_stride +
+                           static_cast<long long>(pr.append_row) * row_stride;
+    for (int idx = threadIdx.x; idx < n_kv * hd; idx += blockDim.x) {
+        const int kvh = idx / hd, d = idx % hd;
+        const float* kin = k_in + static_cast<long long>(pr.io) * kv_stride + kvh * hd;
+        const float kr = rope_elem(kin, d, pr.rope_half, cs, neox != 0);
+        store_kv<DT>(kc, dst0 + idx, kr);
+        store_kv<DT>(vc, dst0 + idx, v_in[static_cast<long long>(pr.io) * kv_stride + idx]);
+    }
+}
+
 // Consumer warps for a ring of `stages` when `split` warps share each tile:
 // every stage must be consumed by one group of warps only, so the number of
 // tile streams (warps / split) divides the ring size.
@@ -423,12 +450,13 @@ std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers
 }
 
 int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
-              float* partials, cudaStream_t stream) {
+              float* partials, cudaStream_t stream, bool prefill = false) {
     if (!kv || !layers || !a) return fail(JX_ERR_INVALID, "null handle, layers or args");
     if (n_layers == 0 || a->n_seqs == 0) return fail(JX_ERR_INVALID, "empty step");
     if (!a->pos || !a->q || !a->k || !a->v) return fail(JX_ERR_INVALID, "null pos/q/k/v");
+    if (prefill && partials) return fail(JX_ERR_INVALID, "prefill writes outputs, not partials");
     std::vector<unsigned char> key = call_key(kv, layers, n_layers, a, partials, stream);
-    if (kv->replay_generation == kv->generation && key == kv->replay_key) {
+    if (!prefill && kv->replay_generation == kv->generation && key == kv->replay_key) {
         DeviceGuard guard(kv->d.device);
         if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
         for (const DecodeLaunch& Lc : kv->replay) {
@@ -455,15 +483,27 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     const jx_kv_desc& D = kv->d;
     std::vector<int> seqs(a->n_seqs);
     {
-        std::vector<char> seen(D.n_seqs, 0);
+        // a step lists each sequence once; a prefill lists a sequence once per
+        // token, each (sequence, position) once
+        std::vector<char> seen(prefill ? 0 : D.n_seqs, 0);
+        std::vector<std::pair<int, int>> rows;
         for (uint32_t s = 0; s < a->n_seqs; ++s) {
-            const int sid = a->seq_ids ? a->seq_ids[s] : static_cast<int>(s);
+            const int sid = a->seq_ids ? a->seq_ids[s] : (prefill ? 0 : static_cast<int>(s));
             if (sid < 0 || static_cast<uint32_t>(sid) >= D.n_seqs)
                 return fail(JX_ERR_INVALID, "sequence id %d outside [0, %u)", sid, D.n_seqs);
-            if (seen[sid]) return fail(JX_ERR_INVALID, "sequence id %d listed twice", sid);
-            seen[sid] = 1;
-            seqs[s] = sid;
             if (a->pos[s] < 0) return fail(JX_ERR_INVALID, "negative position");
+            if (prefill) {
+                rows.emplace_back(sid, a->pos[s]);
+            } else {
+                if (seen[sid]) return fail(JX_ERR_INVALID, "sequence id %d listed twice", sid);
+                seen[sid] = 1;
+            }
+            seqs[s] = sid;
+        }
+        if (prefill) {
+            std::sort(rows.begin(), rows.end());
+            if (std::adjacent_find(rows.begin(), rows.end()) != rows.end())
+                return fail(JX_ERR_INVALID, "a (sequence, position) is listed twice");
         }
     }
     std::vector<char> appended(D.n_layers, 0);
@@ -647,6 +687,26 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         std::memcpy(bytes.data() + cta_off, cta_pair.data(), cta_pair.size() * sizeof(int));
         rc = upload_plan(kv, gi, bytes, stream);
         if (rc) return rc;
+        if (prefill && !pairs.empty()) {
+            // all of this group's rows are stored before any of them is attended
+            const PairRow* dp = static_cast<const PairRow*>(kv->slots[gi].d_buf);
+            const float2* dr = reinterpret_cast<const float2*>(
+                static_cast<unsigned char*>(kv->slots[gi].d_buf) + rope_off);
+            const int np = static_cast<int>(pairs.size());
+            const int nkv = static_cast<int>(a->n_kv_heads);
+#define JX_APPEND(DTV)                                                                      \
+    append_rows_kernel<DTV><<<np, 128, 0, stream>>>(dp, np, dr, width, a->k, a->v,          \
+                                                    a->kv_stride, nkv, hd, neox ? 1 : 0,     \
+                                                    kv->k, kv->v, kv->seq_stride,            \
+                                                    kv->layer_stride, D.row_stride)
+            if (D.dtype == JX_F32) JX_APPEND(DT_F32);
+            else if (D.dtype == JX_BF16) JX_APPEND(DT_BF16);
+            else JX_APPEND(DT_F16T);
+#undef JX_APPEND
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess)
+                return fail(JX_ERR_CUDA, "append launch failed: %s", cudaGetErrorString(e));
+        }
         const long long n_segs = static_cast<long long>(pairs.size()) * n_kv;
         rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * kp * (hd + 2),
                             static_cast<size_t>(std::max<long long>(n_segs, 1)));
@@ -686,6 +746,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.n_stages = stages;
         A.n_consumers = consumers_for(stages, kp);
         A.q_bulk = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
+        A.skip_append = prefill ? 1 : 0;
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;
         A.scratch_floats = static_cast<long long>(kv->scratch_floats);
@@ -717,6 +778,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         launched.push_back(Lc);
     }
     kv->last_launches = launches;
+    if (prefill) return JX_OK;  // not replayed: its append launches are not recorded
     kv->replay_key = std::move(key);
     kv->replay = std::move(launched);
     kv->replay_generation = kv->generation;
@@ -818,14 +880,15 @@ namespace {
 // launches) -- the counterpart of forward_token's attention_ms
 // (transformer.cpp:2499, 2567).
 int timed_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
-               float* partials, cudaStream_t stream) {
-    if (!kv || !kv->opt_timing) return step_impl(kv, layers, n_layers, a, partials, stream);
+               float* partials, cudaStream_t stream, bool prefill = false) {
+    if (!kv || !kv->opt_timing)
+        return step_impl(kv, layers, n_layers, a, partials, stream, prefill);
     DeviceGuard guard(kv->d.device);
     if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
     if (!kv->ev_t0) JX_CUDA(cudaEventCreate(&kv->ev_t0));
     if (!kv->ev_t1) JX_CUDA(cudaEventCreate(&kv->ev_t1));
     JX_CUDA(cudaEventRecord(kv->ev_t0, stream));
-    const int rc = step_impl(kv, layers, n_layers, a, partials, stream);
+    const int rc = step_impl(kv, layers, n_layers, a, partials, stream, prefill);
     JX_CUDA(cudaEventRecord(kv->ev_t1, stream));
     kv->timed = rc == JX_OK;
     return rc;
@@ -1028,6 +1091,11 @@ int jx_attn_step_partial(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_laye
                          const jx_step_args* args, float* partials, void* stream) {
     if (!partials) return fail(JX_ERR_INVALID, "null partials");
     return timed_step(kv, layers, n_layers, args, partials, (cudaStream_t)stream);
+}
+
+int jx_attn_prefill(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                    const jx_step_args* args, void* stream) {
+    return timed_step(kv, layers, n_layers, args, nullptr, (cudaStream_t)stream, true);
 }
 
 int jx_kv_last_step_ms(jx_kv* kv, float* ms) {
