@@ -626,8 +626,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
 
     const long long P = gridDim.x;
     const long long c = blockIdx.x;
-    const long long b0 = a.total * c / P;
-    const long long b1 = a.total * (c + 1) / P;
+    const long long b0 = a.cta_begin ? a.cta_begin[c] : a.total * c / P;
+    const long long b1 = a.cta_begin ? a.cta_begin[c + 1] : a.total * (c + 1) / P;
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
@@ -1083,8 +1083,10 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             bool fence = false;
             for (int k = 0; k < n_split; ++k) {
                 const SplitRec& r = recs[k];
-                const long long c_first = owner_cta(r.seg_start, a.total, P);
-                const long long c_last = owner_cta(r.seg_start + r.len - 1, a.total, P);
+                const long long c_first = a.seg_owner ? a.seg_owner[2 * r.seg]
+                                                      : owner_cta(r.seg_start, a.total, P);
+                const long long c_last = a.seg_owner ? a.seg_owner[2 * r.seg + 1]
+                                                     : owner_cta(r.seg_start + r.len - 1, a.total, P);
                 int last = 0;
                 if (JX_CHECKED(a, r.seg >= 0 && r.seg < a.n_segments &&
                                       c_last + r.seg < P + a.n_segments && c_first >= 0 &&
@@ -1106,8 +1108,11 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         for (int k = 0; k < n_split; ++k) {
             if (!misc[2 + k]) continue;  // the same for every consumer thread
             const SplitRec r = recs[k];
-            merge_split<HD, GS>(a, r, owner_cta(r.seg_start, a.total, P),
-                                owner_cta(r.seg_start + r.len - 1, a.total, P), ctid);
+            const long long c_first =
+                a.seg_owner ? a.seg_owner[2 * r.seg] : owner_cta(r.seg_start, a.total, P);
+            const long long c_last = a.seg_owner ? a.seg_owner[2 * r.seg + 1]
+                                                 : owner_cta(r.seg_start + r.len - 1, a.total, P);
+            merge_split<HD, GS>(a, r, c_first, c_last, ctid);
         }
     }
     (void)JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);

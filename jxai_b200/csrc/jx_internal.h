@@ -28,6 +28,8 @@ static_assert(sizeof(PairRow) == 48, "PairRow layout");
 struct DecodeArgs {
     const PairRow* pairs;
     const int* cta_pair;  // per CTA: the pair holding its first row (or null: binary search)
+    const long long* cta_begin;  // [P+1] slice boundaries, or null: CTA c takes [cN/P, (c+1)N/P)
+    const int* seg_owner;        // with cta_begin: [segments][2] first and last CTA of a segment
     int n_pairs;
     int n_kv;       // kv heads
     int G;          // query heads per kv head

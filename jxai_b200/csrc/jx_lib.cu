@@ -296,6 +296,7 @@ struct jx_kv {
     int opt_ctas_per_sm = 0, opt_stages = 0, opt_grid = 0;
     int opt_pdl = -1;  // programmatic dependent launch: -1 auto, 0 off, 1 on
     int opt_timing = 0;  // 1: events around every step (jx_kv_last_step_ms)
+    float opt_split_penalty_us = -1.0f;  // cost of an extra piece in a CTA's slice; -1: auto
     cudaEvent_t ev_t0 = nullptr, ev_t1 = nullptr;
     bool timed = false;  // a timed step was recorded
     int last_launches = 0;
@@ -435,6 +436,7 @@ std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers
     put(k, a->sliding_window); put(k, a->yarn_scale); put(k, a->rope_neox);
     put(k, partials); put(k, stream);
     put(k, kv->opt_stages); put(k, kv->opt_ctas_per_sm); put(k, kv->opt_grid); put(k, kv->opt_pdl);
+    put(k, kv->opt_split_penalty_us);
     for (uint32_t s = 0; s < a->n_seqs; ++s) {
         put(k, a->pos[s]);
         put(k, a->seq_ids ? a->seq_ids[s] : -1);
@@ -447,6 +449,53 @@ std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers
                             : uint64_t(0));
     }
     return k;
+}
+
+// Rows one CTA streams per microsecond when all P CTAs share HBM evenly
+// (~6.5 TB/s on B200): converts a per-piece time cost into rows.
+double split_rows_per_us(const jx_kv* kv, size_t bytes_per_row, long long P) {
+    (void)kv;
+    if (bytes_per_row == 0 || P <= 0) return 0.0;
+    return 6.5e6 / static_cast<double>(P) / static_cast<double>(bytes_per_row);
+}
+
+// Slice boundaries b[0..P] over the flattened rows (segments start at
+// seg_off[j], seg_off.back() == total) so that every CTA's rows plus
+// `penalty` rows per segment boundary inside its slice come out equal: the
+// smallest per-CTA budget that covers every row, found by bisection.
+std::vector<long long> balanced_split(const std::vector<long long>& seg_off, long long total,
+                                      long long P, double penalty) {
+    std::vector<long long> b(static_cast<size_t>(P) + 1, total);
+    auto layout = [&](double budget_rows, bool write) -> long long {
+        long long x = 0;
+        size_t j = 0;  // seg_off[j] <= x < seg_off[j+1]
+        for (long long c = 0; c < P; ++c) {
+            if (write) b[static_cast<size_t>(c)] = x;
+            double budget = budget_rows;
+            while (x < total) {
+                while (j + 1 < seg_off.size() && seg_off[j + 1] <= x) ++j;
+                const long long seg_end = seg_off[j + 1];
+                const long long avail = seg_end - x;
+                if (static_cast<double>(avail) >= budget) {
+                    x += static_cast<long long>(budget);
+                    break;
+                }
+                x = seg_end;
+                budget -= static_cast<double>(avail) + penalty;
+                if (budget <= 0.0) break;
+            }
+        }
+        if (write) b[static_cast<size_t>(P)] = total;
+        return x;
+    };
+    double lo = static_cast<double>(total) / static_cast<double>(P);
+    double hi = lo + penalty * static_cast<double>(seg_off.size()) + 1.0;
+    for (int it = 0; it < 60 && hi - lo > 0.5; ++it) {
+        const double mid = 0.5 * (lo + hi);
+        if (layout(mid, false) >= total) hi = mid; else lo = mid;
+    }
+    layout(hi, true);
+    return b;
 }
 
 int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
@@ -666,10 +715,45 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         P = std::min<long long>(P, std::max<long long>(1, (total + 63) / 64));
         if (kv->opt_grid) P = kv->opt_grid;
         if (total == 0) P = 1;
+        // Slice boundaries.  Uniform (CTA c takes rows [c*N/P, (c+1)*N/P)) unless
+        // segments are few per CTA: then a CTA whose slice crosses a segment
+        // boundary pays for the extra piece (merge, next q) and gets fewer rows.
+        const long long n_kv_segs = static_cast<long long>(pairs.size()) * n_kv;
+        std::vector<long long> cta_begin;
+        std::vector<int> seg_owner;  // [n_segs][2]: first and last CTA of each segment
+        // measured best on B200 (c1/c2 sweeps): ~5 us per extra piece with the
+        // CUDA-core consumer, ~8 us with the tensor-core one
+        const double penalty_us = kv->opt_split_penalty_us >= 0.0f ? kv->opt_split_penalty_us
+                                                                    : (kv->esz == 2 ? 8.0 : 5.0);
+        const double penalty_rows =
+            penalty_us * split_rows_per_us(kv, static_cast<size_t>(kp) * hd * kv->esz * 2, P);
+        if (penalty_rows > 0.0 && total > 0 && n_kv_segs <= 8 * P) {
+            std::vector<long long> seg_off;  // flattened start of each non-empty segment
+            seg_off.reserve(static_cast<size_t>(n_kv_segs) + 1);
+            for (const PairRow& pr : pairs)
+                for (uint32_t h = 0; h < n_kv; ++h)
+                    if (pr.len > 0) seg_off.push_back(pr.off + static_cast<long long>(h) * pr.len);
+            seg_off.push_back(total);
+            cta_begin = balanced_split(seg_off, total, P, penalty_rows);
+            seg_owner.assign(static_cast<size_t>(n_kv_segs) * 2, 0);
+            size_t c = 0;
+            long long si = 0;
+            for (const PairRow& pr : pairs)
+                for (uint32_t h = 0; h < n_kv; ++h, ++si) {
+                    if (pr.len <= 0) continue;
+                    const long long first = pr.off + static_cast<long long>(h) * pr.len;
+                    const long long last = first + pr.len - 1;
+                    while (c + 1 < static_cast<size_t>(P) && cta_begin[c + 1] <= first) ++c;
+                    size_t d = c;
+                    while (d + 1 < static_cast<size_t>(P) && cta_begin[d + 1] <= last) ++d;
+                    seg_owner[2 * si] = static_cast<int>(c);
+                    seg_owner[2 * si + 1] = static_cast<int>(d);
+                }
+        }
         // each CTA's first pair (the kernel then needs no search to find its slice)
         std::vector<int> cta_pair(static_cast<size_t>(P), 0);
         for (long long c = 0; c < P; ++c) {
-            const long long x = total * c / P;
+            const long long x = cta_begin.empty() ? total * c / P : cta_begin[c];
             int lo = 0, hi = static_cast<int>(pairs.size()) - 1;
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
@@ -681,10 +765,19 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         const size_t rope_off = (pair_bytes + 255) & ~static_cast<size_t>(255);
         const size_t rope_bytes = rope.size() * sizeof(float2);
         const size_t cta_off = (rope_off + rope_bytes + 255) & ~static_cast<size_t>(255);
-        std::vector<unsigned char> bytes(cta_off + cta_pair.size() * sizeof(int), 0);
+        const size_t begin_off =
+            (cta_off + cta_pair.size() * sizeof(int) + 255) & ~static_cast<size_t>(255);
+        const size_t owner_off =
+            (begin_off + cta_begin.size() * sizeof(long long) + 255) & ~static_cast<size_t>(255);
+        std::vector<unsigned char> bytes(owner_off + seg_owner.size() * sizeof(int), 0);
         std::memcpy(bytes.data(), pairs.data(), pair_bytes);
         if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope_bytes);
         std::memcpy(bytes.data() + cta_off, cta_pair.data(), cta_pair.size() * sizeof(int));
+        if (!cta_begin.empty()) {
+            std::memcpy(bytes.data() + begin_off, cta_begin.data(),
+                        cta_begin.size() * sizeof(long long));
+            std::memcpy(bytes.data() + owner_off, seg_owner.data(), seg_owner.size() * sizeof(int));
+        }
         rc = upload_plan(kv, gi, bytes, stream);
         if (rc) return rc;
         if (prefill && !pairs.empty()) {
@@ -717,6 +810,14 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.pairs = static_cast<const PairRow*>(kv->slots[gi].d_buf);
         A.cta_pair = reinterpret_cast<const int*>(static_cast<unsigned char*>(kv->slots[gi].d_buf) +
                                                   cta_off);
+        A.cta_begin = cta_begin.empty() ? nullptr
+                                        : reinterpret_cast<const long long*>(
+                                              static_cast<unsigned char*>(kv->slots[gi].d_buf) +
+                                              begin_off);
+        A.seg_owner = seg_owner.empty() ? nullptr
+                                        : reinterpret_cast<const int*>(
+                                              static_cast<unsigned char*>(kv->slots[gi].d_buf) +
+                                              owner_off);
         A.n_pairs = static_cast<int>(pairs.size());
         A.n_kv = static_cast<int>(n_kv);
         A.G = static_cast<int>(G) * kp;
@@ -1194,7 +1295,9 @@ int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream) {
 }
 
 int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
-    if (!kv || !key || value < 0) return fail(JX_ERR_INVALID, "bad option");
+    if (!kv || !key) return fail(JX_ERR_INVALID, "bad option");
+    if (value < 0 && std::strcmp(key, "pdl") != 0)
+        return fail(JX_ERR_INVALID, "option '%s' takes a non-negative value", key);
     if (!std::strcmp(key, "ctas_per_sm")) kv->opt_ctas_per_sm = value;
     else if (!std::strcmp(key, "stages")) {
         if (value == 1 || value > 16) return fail(JX_ERR_INVALID, "stages must be 2..16");
@@ -1202,6 +1305,8 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
     } else if (!std::strcmp(key, "grid")) kv->opt_grid = value;
     else if (!std::strcmp(key, "pdl")) kv->opt_pdl = value < 0 ? -1 : (value ? 1 : 0);
     else if (!std::strcmp(key, "timing")) kv->opt_timing = value ? 1 : 0;
+    else if (!std::strcmp(key, "split_penalty_us"))
+        kv->opt_split_penalty_us = static_cast<float>(value);
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;
 }
