@@ -222,11 +222,10 @@ JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache, void* v_c
 JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
 
 /* Launch options: "ctas_per_sm", "stages" and "grid" override the launch shape
- * (tuning sweeps; 0 restores the default); "pdl" 1 / 0 / -1 (default: on
- * for steps of at least 2^17 attended rows) turns programmatic dependent
- * launch of the decode kernel on / off / automatic (with it, a step's launch
- * and set-up overlap the previous kernel's tail; its data accesses still wait
- * for that kernel to complete); "timing" 1 records events around every
+ * (tuning sweeps; 0 restores the default); "pdl" 1 (default) / 0 turns
+ * programmatic dependent launch of the decode kernel on / off (with it, a
+ * step's launch and set-up overlap the previous kernel's tail; its data
+ * accesses still wait for that kernel to complete); "timing" 1 records events around every
  * jx_attn_step / jx_attn_step_partial (not while a stream is being captured);
  * "split_penalty_us" (default 5 for fp32 caches, 8 for 16-bit; 0 = uniform
  * slices) is the time an extra piece costs a CTA, used to size slices when

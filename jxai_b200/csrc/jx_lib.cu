@@ -715,9 +715,11 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         P = std::min<long long>(P, std::max<long long>(1, (total + 63) / 64));
         if (kv->opt_grid) P = kv->opt_grid;
         if (total == 0) P = 1;
-        // Slice boundaries.  Uniform (CTA c takes rows [c*N/P, (c+1)*N/P)) unless
-        // segments are few per CTA: then a CTA whose slice crosses a segment
-        // boundary pays for the extra piece (merge, next q) and gets fewer rows.
+        // Slice boundaries.  Uniform (CTA c takes rows [c*N/P, (c+1)*N/P)) for
+        // very many segments per CTA (boundary costs average out, and the
+        // balancing pass is linear in segments); otherwise a CTA whose slice
+        // crosses segment boundaries pays for each extra piece (merge, next q)
+        // and gets fewer rows.
         const long long n_kv_segs = static_cast<long long>(pairs.size()) * n_kv;
         std::vector<long long> cta_begin;
         std::vector<int> seg_owner;  // [n_segs][2]: first and last CTA of each segment
@@ -727,7 +729,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                                                                     : (kv->esz == 2 ? 8.0 : 5.0);
         const double penalty_rows =
             penalty_us * split_rows_per_us(kv, static_cast<size_t>(kp) * hd * kv->esz * 2, P);
-        if (penalty_rows > 0.0 && total > 0 && n_kv_segs <= 8 * P) {
+        if (penalty_rows > 0.0 && total > 0 && n_kv_segs <= 64 * P) {
             std::vector<long long> seg_off;  // flattened start of each non-empty segment
             seg_off.reserve(static_cast<size_t>(n_kv_segs) + 1);
             for (const PairRow& pr : pairs)
@@ -866,10 +868,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         Lc.dtype = D.dtype;
         Lc.grid = static_cast<int>(P);
         Lc.stages = stages;
-        // Auto: on for steps that stream (c2: -2.6 %, c2 bf16: -4.5 % per step
-        // measured), off for latency-bound steps of a few tiles per CTA
-        // (c1, 12.6 MB: +5 % with it).
-        Lc.pdl = kv->opt_pdl >= 0 ? kv->opt_pdl : (total >= (1ll << 17) ? 1 : 0);
+        // Default on: measured -3 % (c2), -5 % (c2 bf16), -7 % (c1) per step.
+        Lc.pdl = kv->opt_pdl >= 0 ? kv->opt_pdl : 1;
         Lc.stream = stream;
         if (total == 0 && !partial) continue;
         const cudaError_t e = decode_launch(Lc);

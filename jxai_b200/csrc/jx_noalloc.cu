@@ -319,7 +319,7 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     Lc.dtype = D.dtype;
     Lc.grid = static_cast<int>(P);
     Lc.stages = stages;
-    Lc.pdl = total >= (1ll << 17) ? 1 : 0;  // as jx_attn_step's automatic choice
+    Lc.pdl = 1;  // as jx_attn_step's default
     Lc.stream = stream;
     e = decode_launch(Lc);
     if (e != cudaSuccess) return nfail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
