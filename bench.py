@@ -347,18 +347,25 @@ def run_ours(args, rank, world, local_rank):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
-        qh = torch.empty(r.q.shape, pin_memory=True)
-        kh = torch.empty(r.k.shape, pin_memory=True)
-        vh = torch.empty(r.v.shape, pin_memory=True)
+        # q, k and v of a step side by side in one pinned host buffer (one H2D
+        # copy per step, as an engine staging its projections would), the
+        # output read back with one D2H copy
+        nq, nk = r.q.numel(), r.k.numel()
+        inh = torch.empty(nq + 2 * nk, pin_memory=True)
+        inh[:nq].copy_(r.q.reshape(-1).cpu())
+        inh[nq:nq + nk].copy_(r.k.reshape(-1).cpu())
+        inh[nq + nk:].copy_(r.v.reshape(-1).cpu())
+        ind = torch.empty(nq + 2 * nk, device=r.q.device)
+        qd = ind[:nq].view(r.q.shape)
+        kd = ind[nq:nq + nk].view(r.k.shape)
+        vd = ind[nq + nk:].view(r.v.shape)
         oh = torch.empty(r.out.shape, pin_memory=True)
-        qh.copy_(r.q.cpu()); kh.copy_(r.k.cpu()); vh.copy_(r.v.cpu())
-        qd, kd, vd, od = (torch.empty_like(x) for x in (r.q, r.k, r.v, r.out))
+        od = torch.empty_like(r.out)
+        qh, kh, vh = inh[:nq], inh[nq:nq + nk], inh[nq + nk:]
         e2e_plan = r.plan(qd, kd, vd, od)
 
         def e2e_step():
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
+            ind.copy_(inh, non_blocking=True)
             r.kernel(e2e_plan)
             r.finish(od)
             oh.copy_(od, non_blocking=True)
@@ -382,7 +389,7 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": round(total_kv * K / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h),
-               "path": "pinned host q/k/v -> H2D -> jx_attn_step (C ABI) -> D2H attn_out"}
+               "path": "pinned host q|k|v -> one H2D -> jx_attn_step (C ABI) -> one D2H attn_out"}
 
     # ---- CPU baseline (rank 0, N=1)
     cpu = None
