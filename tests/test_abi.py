@@ -87,3 +87,18 @@ def test_no_gpu_means_a_loud_failure():
     with pytest.raises(jx.JxError) as e:
         jx.KVCache(1, 1, 16, 64, "f32")
     assert e.value.code == _lib.JX_ERR_CUDA
+
+
+def test_cmake_project_configures():
+    # CMakeLists.txt builds the same library for C++ engines that use CMake
+    import shutil
+    import tempfile
+    cmake = shutil.which("cmake")
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if cmake is None or not os.path.exists(nvcc):
+        pytest.skip("cmake or nvcc not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    with tempfile.TemporaryDirectory() as td:
+        r = subprocess.run([cmake, "-S", root, "-B", td, f"-DCMAKE_CUDA_COMPILER={nvcc}"],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stderr[-2000:]
