@@ -5,17 +5,24 @@
 // RoPE on q and k, the append of k and v at `pos`, and grouped-query attention
 // over every attended cache row.  Design:
 //
-//  * Work space.  Rows are flattened over (pair, kv head, row); each of the P
-//    persistent CTAs takes an equal contiguous slice of that space, so bytes
-//    are balanced across SMs however ragged the sequences are.  A slice cuts
-//    segments (one segment = one (pair, kv head)) into pieces.
+//  * Work space.  Rows are flattened over (pair, segment, row), a segment being
+//    one kv head of a pair (two for 16-bit caches with short head rows); each
+//    of the P persistent CTAs takes a contiguous slice of that space -- equal
+//    in rows, or (with few segments per CTA) sized on the host so that rows
+//    plus a cost per extra piece come out equal -- so bytes are balanced
+//    across SMs however ragged the sequences are.  A slice cuts segments into
+//    pieces.
 //  * Pipeline.  Warp 4 is the producer: it streams 32-row K and V tiles of the
 //    current piece into a ring of shared-memory stages with 4-D TMA tile loads
-//    (128-byte swizzle, no multicast), completion tracked by mbarriers.
-//    Warps 0-3 are consumers; tile k goes to warp k % C with the ring size a
-//    multiple of C, so every use of a given stage is consumed by the same warp,
-//    in order.  (A stage whose successive uses went to different warps could be
-//    waited on two phases ahead, which mbarrier parity cannot tell apart.)
+//    (128-byte swizzle, no multicast), completion tracked by mbarriers, and
+//    bulk-copies each piece's q and RoPE row into one of two q slots.
+//    Warps 0-3 are consumers; tile k goes to stream k % S (S = consumer warps /
+//    warps per tile) with the ring size a multiple of S, so every use of a
+//    given stage is consumed by the same warps, in order.  (A stage whose
+//    successive uses went to different warps could be waited on two phases
+//    ahead, which mbarrier parity cannot tell apart.)  The kernel lets the next
+//    kernel of the stream launch early (programmatic dependent launch) and
+//    waits for the previous one before touching data.
 //  * fp32 caches: math on CUDA cores (~1 flop per KV byte at group 4, well
 //    under the FMA rate at HBM speed).  QK: lane = cache row, dot product over
 //    head_dim in ascending order with fused multiply-adds (the reference's
@@ -30,15 +37,17 @@
 //    its own consumer warp.
 //  * Merge.  At the end of a piece the four warps' (m, l, o) are merged through
 //    shared memory.  A piece that is a whole segment writes the normalised
-//    output directly; otherwise it writes a partial to scratch and the last
-//    CTA to finish the segment (atomic counter, no waiting) merges all of them
-//    by log-sum-exp and resets the counter.
+//    output directly; otherwise it writes a partial to scratch and counts
+//    itself in on the segment's counter (no waiting); the CTA that counts in
+//    last merges all partials by log-sum-exp after its own last piece and
+//    resets the counter.
 //  * Append.  The CTA that owns a segment's newest row rotates and stores that
 //    row's k and v slice (producer warp), fences the generic->async proxy, and
 //    only then loads the tile holding it.
 //
 // Template parameters: HD = head_dim, GP = query heads per kv head rounded up
-// to 1/2/4/8, DT = cache element type (DT_F32 / DT_BF16 / DT_F16T).
+// to 1/2/4/8, DT = cache element type (DT_F32 / DT_BF16 / DT_F16T), KP = kv
+// heads per tile row (1, or 2 for 16-bit caches with short head rows).
 #pragma once
 
 #include "jx_device.cuh"

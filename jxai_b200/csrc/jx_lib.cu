@@ -1,8 +1,10 @@
 // jx_lib.cu -- host side of libjxattn.so: the C ABI declared in
 // include/jx_attn.h.  Owns the device KV cache (the B200 counterpart of
-// KVCacheSlot, include/transformer.h:115-131), turns each decode step into a
-// flattened work plan, and launches the fused kernel (jx_decode.cuh), plus the
-// log-sum-exp merge of sequence shards and the seeded fill used by benches.
+// KVCacheSlot, include/transformer.h:115-131), turns each decode step (or
+// prefill) into a flattened work plan with balanced CTA slices, and launches
+// the fused kernel (jx_decode.cuh); plus the log-sum-exp merge of sequence
+// shards, the NCCL-sharded step, the prefill append pass and the seeded fill
+// used by benches.
 #include <cudaTypedefs.h>
 #include <dlfcn.h>
 #include <nccl.h>  // types and enum values only: the functions are resolved at run time

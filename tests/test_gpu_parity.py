@@ -25,7 +25,8 @@ def _torch():
 
 def run_case(dtype, n_heads, n_kv, hd, lengths, neox=True, n_layers=2, softcap=0.0, window=0,
              swa_layers=(), grid=0, seed=0, capacity=None, row_pad=0, rope_dim=None,
-             yarn=1.0, rope_freqs=None, check_fp32_ref=False, q_scale=1.0, poison_tail=False):
+             yarn=1.0, rope_freqs=None, check_fp32_ref=False, q_scale=1.0, poison_tail=False,
+             options=None):
     import jxai_b200 as jx
     torch = _torch()
     rng = np.random.default_rng(seed)
@@ -52,6 +53,8 @@ def run_case(dtype, n_heads, n_kv, hd, lengths, neox=True, n_layers=2, softcap=0
     cache = jx.KVCache(n_seqs, n_layers, cap, rs, dtype)
     if grid:
         cache.set_option("grid", grid)
+    for key, val in (options or {}).items():
+        cache.set_option(key, val)
     for s in range(n_seqs):
         for l in range(n_layers):
             cache.write_rows(s, l, 0, 0, kc[s, l])
@@ -94,9 +97,19 @@ def test_step_matches_oracle(dtype, neox, shape):
 
 
 @pytest.mark.parametrize("grid", [1, 3, 7, 64])
-def test_split_pieces_merge(grid):
-    # forcing few/many CTAs puts segment boundaries everywhere: multi-piece merges
-    run_case(F32, 32, 8, 64, [5, 97, 300, 1], grid=grid, n_layers=3)
+@pytest.mark.parametrize("penalty", [None, 0, 40])
+def test_split_pieces_merge(grid, penalty):
+    # forcing few/many CTAs puts segment boundaries everywhere: multi-piece
+    # merges; slices balanced by the default per-piece cost, uniform (0) or a
+    # large cost (40 us: several short or empty slices)
+    opts = {} if penalty is None else {"split_penalty_us": penalty}
+    run_case(F32, 32, 8, 64, [5, 97, 300, 1], grid=grid, n_layers=3, options=opts)
+    run_case(BF16, 32, 8, 64, [5, 97, 300, 1], grid=grid, n_layers=3, options=opts)
+
+
+@pytest.mark.parametrize("pdl", [0, 1])
+def test_programmatic_launch_off_and_on(pdl):
+    run_case(F32, 32, 8, 64, [200, 33], grid=7, options={"pdl": pdl})
 
 
 @pytest.mark.parametrize("T", [1, 2, 31, 32, 33, 63, 64, 65, 511, 512])
