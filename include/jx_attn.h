@@ -227,9 +227,9 @@ JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
  * step's launch and set-up overlap the previous kernel's tail; its data
  * accesses still wait for that kernel to complete); "timing" 1 records events around every
  * jx_attn_step / jx_attn_step_partial (not while a stream is being captured);
- * "split_penalty_us" (default 5 for fp32 caches, 8 for 16-bit; 0 = uniform
- * slices) is the time an extra piece costs a CTA, used to size slices when
- * segments are few per CTA. */
+ * "split_penalty_us" (-1 = default: 5 for fp32 caches, 8 for 16-bit; 0 =
+ * uniform slices) is the time an extra piece costs a CTA, used to size the
+ * CTAs' slices. */
 JX_API int jx_kv_set_option(jx_kv* kv, const char* key, int value);
 
 /* Device time of the last step recorded with option "timing" (waits for it):

@@ -90,12 +90,13 @@ struct SmemLayout {
     static constexpr int p_bytes = DT == DT_F32 ? kConsumerWarps * kTileRows * GS * 4 : 0;
     static constexpr int o_bytes = kConsumerWarps * GS * HD * 4;
     static constexpr int ml_bytes = kConsumerWarps * GS * 2 * 4;
-    static constexpr int misc_bytes = 16 + 2 * 32;      // flags + two split-piece records
+    static constexpr int lohi_bytes = 2 * GS * 4;       // per-column row limits (prefill blocks)
+    static constexpr int misc_bytes = 16 + 2 * 48;      // flags + two split-piece records
     static constexpr int n_extra_bars = 4;              // q full[2], q empty[2]
     static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
     static __host__ __device__ constexpr int bars_offset(int ns) {
         return stages_bytes(ns) + q_bytes + qraw_bytes + rope_bytes + p_bytes + o_bytes +
-               ml_bytes + misc_bytes;
+               ml_bytes + lohi_bytes + misc_bytes;
     }
     static __host__ __device__ constexpr int total(int ns) {
         return bars_offset(ns) + (ns * 2 + n_extra_bars) * 8 + 1024;  // + alignment slack
@@ -232,8 +233,11 @@ struct SplitRec {
     int io;               // q/out row of the pair
     int kvh;              // kv head (of the segment) within the pair
     int early;            // 1: counted in when the piece ended (more pieces followed)
+    int nq;               // tokens of a prefill block (1 otherwise)
+    int io_step;          // io distance between the block's tokens
+    int pad[2];
 };
-static_assert(sizeof(SplitRec) == 32, "SplitRec layout");
+static_assert(sizeof(SplitRec) == 48, "SplitRec layout");
 
 // Last-arriver merge of segment `r`: the partials of CTAs c_first..c_last are
 // combined by log-sum-exp and the output written.  Each consumer thread owns
@@ -247,6 +251,7 @@ __device__ __forceinline__ void merge_split(const DecodeArgs& a, const SplitRec&
     constexpr int QC = (24 / E) < 1 ? 1 : ((24 / E) > 8 ? 8 : (24 / E));
     const int np = static_cast<int>(c_last - c_first + 1);
     const int Gn = a.G;
+    const int ncol = Gn * (r.nq > 1 ? r.nq : 1);  // (token, head) columns
     const long long step = static_cast<long long>(GS) * (HD + 2);
     const float* base_p = a.scratch + (c_first + r.seg) * step;
     float M[E], Ls[E], O[E];
@@ -265,7 +270,7 @@ __device__ __forceinline__ void merge_split(const DecodeArgs& a, const SplitRec&
             const float* src = base_p + static_cast<long long>(g) * (HD + 2);
 #pragma unroll
             for (int qq = 0; qq < QC; ++qq) {
-                const bool ok = idx < Gn * HD && q0 + qq < np;
+                const bool ok = idx < ncol * HD && q0 + qq < np;
                 const float* pq = src + (q0 + qq) * step;
                 mv[e][qq] = ok ? __ldcg(pq + HD) : -INFINITY;
                 lv[e][qq] = ok ? __ldcg(pq + HD + 1) : 0.0f;
@@ -293,9 +298,10 @@ __device__ __forceinline__ void merge_split(const DecodeArgs& a, const SplitRec&
 #pragma unroll
     for (int e = 0; e < E; ++e) {
         const int idx = ctid + e * kConsumerThreads;
-        if (idx < Gn * HD) {
+        if (idx < ncol * HD) {
             const int g = idx / HD, d = idx % HD;
-            emit_final<HD>(a, r.io, r.kvh * Gn + g, d, M[e], Ls[e], O[e]);
+            const int j = g / Gn, h = g - j * Gn;
+            emit_final<HD>(a, r.io + j * r.io_step, r.kvh * Gn + h, d, M[e], Ls[e], O[e]);
         }
     }
 }
@@ -328,6 +334,8 @@ struct MmaWarp {
     float o[KS][NBC][4];      // O^T accumulators
     float m[2], l[2];         // running max / lane-partial sum per slot
     float s_unscale;          // 2^-shift of the fp16 q scaling (1 for bf16)
+    bool blocked;             // prefill block: per-slot attended rows [row_lo, row_hi]
+    int row_lo[2], row_hi[2];
 
     // Sum of a value over the columns that hold the same head (see above).
     __device__ __forceinline__ static float col_sum(const float (&x)[NBC][4], int r) {
@@ -349,9 +357,19 @@ struct MmaWarp {
 
     // q_s: rotated q of the segment's KP*GP heads, [head][HD]; this warp takes
     // kv head `kp_` of the tile row and its GP query heads.
-    __device__ __forceinline__ void begin_piece(const float* q_s, int lane, int kp_) {
+    __device__ __forceinline__ void begin_piece(const float* q_s, int lane, int kp_,
+                                                const int* lohi) {
         kp = kp_;
         const int g = lane >> 2, t = lane & 3;
+        blocked = lohi != nullptr;
+        if (blocked) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int hs = kp * GP + (2 * t + j) % GP;
+                row_lo[j] = lohi[hs];
+                row_hi[j] = lohi[KP * GP + hs];
+            }
+        }
         float x[KS][NBC][4];
         float mx = 0.0f;
 #pragma unroll
@@ -406,8 +424,8 @@ struct MmaWarp {
 
     // One tile of kTileRows rows; rows [nvalid, kTileRows) are not attended.
     __device__ __forceinline__ void tile(uint32_t Kt, unsigned char* Vt_ptr, uint32_t Vt,
-                                         int nvalid, int lane, float scale, float softcap,
-                                         float inv_cap) {
+                                         int nvalid, int row_first, int lane, float scale,
+                                         float softcap, float inv_cap) {
         const int g = lane >> 2, t = lane & 3;
         const int i8 = lane >> 3, r8 = lane & 7;
         const int cb = kp * HD * 2;  // this kv head's first byte in a tile row
@@ -452,7 +470,11 @@ struct MmaWarp {
             for (int r = 0; r < 4; ++r) {
                 float sc = __fmul_rn(col_sum(acc[mb], r) * s_unscale, scale);
                 if (softcap > 0.0f) sc = __fmul_rn(softcap, tanhf(__fmul_rn(sc, inv_cap)));
-                s[mb][r] = mb * 16 + (r >> 1) * 8 + g < nvalid ? sc : -INFINITY;
+                const int rt = mb * 16 + (r >> 1) * 8 + g;  // row within the tile
+                bool keep = rt < nvalid;
+                if (blocked)
+                    keep = keep && row_first + rt >= row_lo[r & 1] && row_first + rt <= row_hi[r & 1];
+                s[mb][r] = keep ? sc : -INFINITY;
             }
         float alpha[2];
 #pragma unroll
@@ -471,7 +493,7 @@ struct MmaWarp {
         for (int mb = 0; mb < 2; ++mb)
 #pragma unroll
             for (int r = 0; r < 4; ++r) {
-                p[mb][r] = ex2_approx((s[mb][r] - m[r & 1]) * kLog2e);
+                p[mb][r] = s[mb][r] == -INFINITY ? 0.0f : ex2_approx((s[mb][r] - m[r & 1]) * kLog2e);
                 ls[r & 1] += p[mb][r];
             }
 #pragma unroll
@@ -598,7 +620,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     float* p_s = reinterpret_cast<float*>(rope_s) + L::rope_bytes / 4;
     float* o_s = p_s + L::p_bytes / 4;
     float* ml_s = o_s + L::o_bytes / 4;
-    int* misc = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);  // [1] abort, [2..3] last flags
+    int* lohi_s = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);  // [GS] lo, [GS] hi
+    int* misc = lohi_s + 2 * GS;  // [1] abort, [2..3] last flags
     SplitRec* recs = reinterpret_cast<SplitRec*>(misc + 4);     // [2]
     // full[s] at bars+8s, empty[s] at bars+8(NS+s), q full[2], q empty[2] after them
     const uint32_t bars = base_u32 + L::bars_offset(NS);
@@ -801,6 +824,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     while (it.next()) {
         const PairRow& pr = it.pr;
         const int kvh = it.kvh;
+        const bool blocked = pr.nq > 1;  // a prefill block of several tokens
 
         // q rotation for this segment's query group -> q_s (padded heads = 0).
         // Every reader of q_s for the previous piece passed the barrier that
@@ -818,17 +842,40 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             named_bar_sync(1, kConsumerThreads);
             if (ctid == 0) mbar_arrive(qempty + 8 * qs);
         } else {
+        // q straight from global memory; a prefill block's column g is head
+        // g % G of token g / G (its own q row and cos/sin row)
         named_bar_sync(1, kConsumerThreads);
-        if (JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
-                              pr.rope_row < a.n_rope_rows && (kvh + 1) * a.G <= a.n_heads,
+        const int nq = pr.nq > 1 ? pr.nq : 1;
+        if (JX_CHECKED(a, pr.io >= 0 && pr.io + (nq - 1) * pr.io_step < a.n_io &&
+                              pr.rope_row >= 0 && pr.rope_row + nq - 1 < a.n_rope_rows &&
+                              (kvh + 1) * a.G <= a.n_heads,
                        50, pr.io, pr.rope_row, kvh)) {
-            const float* qin = a.q + static_cast<long long>(pr.io) * a.q_stride +
-                               static_cast<long long>(kvh) * a.G * HD;
-            const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
             for (int idx = ctid; idx < GS * HD; idx += kConsumerThreads) {
                 const int g = idx / HD, d = idx % HD;
-                q_s[idx] = g < a.G ? rope_elem(qin + g * HD, d, pr.rope_half, cs, a.neox != 0)
-                                   : 0.0f;
+                const int j = g / a.G, h = g - j * a.G;
+                float val = 0.0f;
+                if (j < nq) {
+                    const float* qin = a.q +
+                                       static_cast<long long>(pr.io + j * pr.io_step) * a.q_stride +
+                                       (static_cast<long long>(kvh) * a.G + h) * HD;
+                    const float2* cs =
+                        a.rope + static_cast<long long>(pr.rope_row + j) * (HD / 2);
+                    val = rope_elem(qin, d, pr.rope_half, cs, a.neox != 0);
+                }
+                q_s[idx] = val;
+            }
+            if (nq > 1) {
+                // per-column attended rows: token j sees [lo, tok_row0 + j]
+                for (int g = ctid; g < GS; g += kConsumerThreads) {
+                    const int j = g / a.G;
+                    int lo = 1, hi = 0;  // padded column: nothing
+                    if (j < nq) {
+                        hi = pr.tok_row0 + j;
+                        lo = pr.window > 0 ? max(pr.row0, hi - pr.window + 1) : pr.row0;
+                    }
+                    lohi_s[g] = lo;
+                    lohi_s[GS + g] = hi;
+                }
             }
         }
         named_bar_sync(1, kConsumerThreads);
@@ -845,7 +892,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
 
         float m[GS], l[GS], o[GS][G::DPL];
         if constexpr (kMma) {
-            mw.begin_piece(q_s, lane, warp % kSplit);
+            mw.begin_piece(q_s, lane, warp % kSplit, blocked ? lohi_s : nullptr);
         } else {
 #pragma unroll
             for (int g = 0; g < GS; ++g) {
@@ -869,7 +916,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             if constexpr (kMma) {
                 const uint32_t ku = base_u32 + my_stage * 2 * G::TILEB;
                 mw.tile(ku, base + my_stage * 2 * G::TILEB + G::TILEB, ku + G::TILEB, nvalid,
-                        lane, scale, softcap, inv_cap);
+                        pr.row0 + it.r + t * kTileRows, lane, scale, softcap, inv_cap);
             } else {
 
             // ---- scores: lane = row
@@ -903,6 +950,12 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                     if (softcap > 0.0f) sc = __fmul_rn(softcap, tanhf(__fmul_rn(sc, inv_cap)));
                     s[g] = sc;
                 }
+                if (blocked) {  // prefill block: each token's causal / window limits
+                    const int rowl = pr.row0 + it.r + t * kTileRows + lane;
+#pragma unroll
+                    for (int g = 0; g < GS; ++g)
+                        if (rowl < lohi_s[g] || rowl > lohi_s[GS + g]) s[g] = -INFINITY;
+                }
             } else {
 #pragma unroll
                 for (int g = 0; g < GS; ++g) s[g] = -INFINITY;
@@ -915,7 +968,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 const float mt = warp_max(s[g]);
                 const float mn = fmaxf(m[g], mt);
                 const float alpha = m[g] == -INFINITY ? 0.0f : ex2_approx((m[g] - mn) * kLog2e);
-                const float p = lane < nvalid ? ex2_approx((s[g] - mn) * kLog2e) : 0.0f;
+                const float p =
+                    (lane < nvalid && s[g] != -INFINITY) ? ex2_approx((s[g] - mn) * kLog2e) : 0.0f;
                 l[g] = l[g] * alpha + p;
 #pragma unroll
                 for (int k = 0; k < G::DPL; ++k) o[g][k] *= alpha;
@@ -1037,7 +1091,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         const bool whole = it.r == 0 && it.n == pr.len;
         const long long seg = static_cast<long long>(it.pi) * a.n_kv + kvh;
         const long long slot = c + seg;
-        for (int idx = ctid; idx < a.G * HD; idx += kConsumerThreads) {
+        const int ncol = a.G * (blocked ? pr.nq : 1);  // (token, head) columns
+        for (int idx = ctid; idx < ncol * HD; idx += kConsumerThreads) {
             const int g = idx / HD, d = idx % HD;
             float M = -INFINITY;
 #pragma unroll
@@ -1051,7 +1106,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 O += o_s[(w * GS + g) * HD + d] * f;
             }
             if (whole) {
-                emit_final<HD>(a, pr.io, kvh * a.G + g, d, M, Lsum, O);
+                const int j = g / a.G, h = g - j * a.G;
+                emit_final<HD>(a, pr.io + j * pr.io_step, kvh * a.G + h, d, M, Lsum, O);
             } else if (JX_CHECKED(a, (slot + 1) * GS * (HD + 2) <= a.scratch_floats, 60, slot, seg, 0)) {
                 float* dst = a.scratch + (slot * GS + g) * (HD + 2);
                 dst[d] = O;
@@ -1074,6 +1130,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                     r.io = pr.io;
                     r.kvh = kvh;
                     r.early = early ? 1 : 0;
+                    r.nq = blocked ? pr.nq : 1;
+                    r.io_step = pr.io_step;
                 }
                 if (early) pending_seg = seg;  // counted in after the next piece's first barrier
                 ++n_split;

@@ -21,9 +21,18 @@ struct PairRow {
     int append_row;   // local row receiving this step's k/v, or -1
     int rope_row;     // row of the cos/sin table for (rope config, pos)
     int rope_half;    // rotated pairs per head = min(head_dim, rope_dim) / 2
+    // A prefill block: nq > 1 consecutive tokens of one sequence share the
+    // pair (their rows stream once for all of them).  Token j has q/out row
+    // io + j*io_step, position row tok_row0 + j, cos/sin row rope_row + j, and
+    // attends local rows [max(row0, tok_row0 + j - window + 1), tok_row0 + j]
+    // (window 0: from row0).  nq <= 1: an ordinary pair.
+    int nq;
+    int io_step;
+    int tok_row0;
+    int window;
     int pad[2];
 };
-static_assert(sizeof(PairRow) == 48, "PairRow layout");
+static_assert(sizeof(PairRow) == 64, "PairRow layout");
 
 struct DecodeArgs {
     const PairRow* pairs;

@@ -140,16 +140,20 @@ __global__ void append_rows_kernel(const PairRow* __restrict__ pairs, int n_pair
     if (i >= n_pairs) return;
     const PairRow pr = pairs[i];
     if (pr.append_row < 0) return;
-    const float2* cs = rope + static_cast<long long>(pr.rope_row) * rope_width;
-    const long long dst0 = static_cast<long long>(pr.seq) * seq_stride +
-                           static_cast<long long>(pr.cache_layer) * layer_stride +
-                           static_cast<long long>(pr.append_row) * row_stride;
-    for (int idx = threadIdx.x; idx < n_kv * hd; idx += blockDim.x) {
-        const int kvh = idx / hd, d = idx % hd;
-        const float* kin = k_in + static_cast<long long>(pr.io) * kv_stride + kvh * hd;
-        const float kr = rope_elem(kin, d, pr.rope_half, cs, neox != 0);
-        store_kv<DT>(kc, dst0 + idx, kr);
-        store_kv<DT>(vc, dst0 + idx, v_in[static_cast<long long>(pr.io) * kv_stride + idx]);
+    const int nq = pr.nq > 1 ? pr.nq : 1;  // tokens of a prefill block
+    for (int j = 0; j < nq; ++j) {
+        const float2* cs = rope + static_cast<long long>(pr.rope_row + j) * rope_width;
+        const long long io = pr.io + static_cast<long long>(j) * pr.io_step;
+        const long long dst0 = static_cast<long long>(pr.seq) * seq_stride +
+                               static_cast<long long>(pr.cache_layer) * layer_stride +
+                               static_cast<long long>(pr.append_row + j) * row_stride;
+        for (int idx = threadIdx.x; idx < n_kv * hd; idx += blockDim.x) {
+            const int kvh = idx / hd, d = idx % hd;
+            const float* kin = k_in + io * kv_stride + kvh * hd;
+            const float kr = rope_elem(kin, d, pr.rope_half, cs, neox != 0);
+            store_kv<DT>(kc, dst0 + idx, kr);
+            store_kv<DT>(vc, dst0 + idx, v_in[io * kv_stride + idx]);
+        }
     }
 }
 
@@ -461,13 +465,42 @@ double split_rows_per_us(const jx_kv* kv, size_t bytes_per_row, long long P) {
     return 6.5e6 / static_cast<double>(P) / static_cast<double>(bytes_per_row);
 }
 
-// Slice boundaries b[0..P] over the flattened rows (segments start at
+// Slice boundaries b[0..P] over the flattened rows (segment j starts at
 // seg_off[j], seg_off.back() == total) so that every CTA's rows plus
-// `penalty` rows per segment boundary inside its slice come out equal: the
-// smallest per-CTA budget that covers every row, found by bisection.
+// `penalty` rows per extra piece (each segment boundary inside its slice)
+// come out equal.
+//  * Few segments per CTA: the smallest per-CTA budget that covers every row,
+//    by bisection (each step a walk over the CTAs and segments).
+//  * Many (a prefill's thousands of short segments): one pass -- with
+//    F(x) = x + penalty * (segment starts <= x), CTA c takes
+//    [F^-1(c*C/P), F^-1((c+1)*C/P)), C = F(total).  Here a CTA's share is
+//    much larger than one penalty, so no CTA falls inside a single step of F
+//    (which would leave it empty).
 std::vector<long long> balanced_split(const std::vector<long long>& seg_off, long long total,
                                       long long P, double penalty) {
     std::vector<long long> b(static_cast<size_t>(P) + 1, total);
+    const size_t m = seg_off.size() - 1;  // segments
+    b[0] = 0;
+    if (m == 0 || P <= 1) return b;
+    if (m > static_cast<size_t>(64 * P)) {
+        std::vector<double> F(m);  // F just after segment j's start
+        for (size_t j = 0; j < m; ++j)
+            F[j] = static_cast<double>(seg_off[j]) + penalty * static_cast<double>(j + 1);
+        const double C = static_cast<double>(total) + penalty * static_cast<double>(m);
+        for (long long c = 1; c < P; ++c) {
+            const double target = C * static_cast<double>(c) / static_cast<double>(P);
+            const size_t j = static_cast<size_t>(
+                std::upper_bound(F.begin(), F.end(), target) - F.begin());
+            long long x = 0;
+            if (j > 0) {
+                const size_t sj = j - 1;
+                x = std::min(seg_off[sj] + static_cast<long long>(target - F[sj]), seg_off[sj + 1]);
+            }
+            b[static_cast<size_t>(c)] = std::max(x, b[static_cast<size_t>(c - 1)]);
+        }
+        b[static_cast<size_t>(P)] = total;
+        return b;
+    }
     auto layout = [&](double budget_rows, bool write) -> long long {
         long long x = 0;
         size_t j = 0;  // seg_off[j] <= x < seg_off[j+1]
@@ -491,7 +524,7 @@ std::vector<long long> balanced_split(const std::vector<long long>& seg_off, lon
         return x;
     };
     double lo = static_cast<double>(total) / static_cast<double>(P);
-    double hi = lo + penalty * static_cast<double>(seg_off.size()) + 1.0;
+    double hi = lo + penalty * static_cast<double>(m) + 1.0;
     for (int it = 0; it < 60 && hi - lo > 0.5; ++it) {
         const double mid = 0.5 * (lo + hi);
         if (layout(mid, false) >= total) hi = mid; else lo = mid;
@@ -609,7 +642,13 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     for (size_t gi = 0; gi < groups.size(); ++gi) {
         const Group& grp = groups[gi];
         const int hd = grp.hd;
-        const int kp = kv_pack(hd, kv->esz, a->n_kv_heads, G, gp);
+        // Prefill blocks: up to 8/G consecutive tokens of a sequence share one
+        // pair (8 query columns: token x head), so their rows stream once.
+        const int nq_max =
+            (prefill && gp == static_cast<int>(G) && G <= 4) ? 8 / static_cast<int>(G) : 1;
+        const bool blocks = nq_max > 1;
+        const int gp_l = blocks ? 8 : gp;  // kernel query columns per segment
+        const int kp = blocks ? 1 : kv_pack(hd, kv->esz, a->n_kv_heads, G, gp);
         const uint32_t n_kv = a->n_kv_heads / kp;  // segments per (sequence, layer) pair
         const int box_kind = kp * hd * kv->esz >= 128 ? 0 : 1;
         int rc = encode_maps(kv, box_kind);
@@ -621,22 +660,38 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
             rope_ids;
         std::vector<float2> rope;
         const int width = hd / 2;
+        int n_rope_rows = 0;
+        // step rows grouped into blocks (first row, tokens): single rows, or
+        // in prefill runs of rows of one sequence at consecutive positions
+        std::vector<std::pair<uint32_t, uint32_t>> blk;
+        for (uint32_t r = 0; r < a->n_seqs;) {
+            uint32_t nb = 1;
+            if (blocks)
+                while (nb < static_cast<uint32_t>(nq_max) && r + nb < a->n_seqs &&
+                       seqs[r + nb] == seqs[r] &&
+                       a->pos[r + nb] == a->pos[r] + static_cast<int32_t>(nb))
+                    ++nb;
+            blk.emplace_back(r, nb);
+            r += nb;
+        }
         long long off = 0;
-        for (uint32_t s = 0; s < a->n_seqs; ++s) {
-            const uint32_t pos = static_cast<uint32_t>(a->pos[s]);
+        for (const auto& bk : blk) {
+            const uint32_t s = bk.first, nb = bk.second;
+            const uint32_t pos = static_cast<uint32_t>(a->pos[s]);  // first token
+            const uint32_t pos_last = pos + nb - 1;
             for (uint32_t l : grp.layers) {
                 const jx_layer_desc& L = layers[l];
                 const uint32_t W = a->sliding_window;
                 const uint64_t t0 = (L.is_swa && W > 0 && pos >= W) ? pos - W + 1 : 0;
                 const uint64_t lo = std::max<uint64_t>(t0, D.pos_base);
-                const uint64_t hi =
-                    std::min<uint64_t>(pos, static_cast<uint64_t>(D.pos_base) + D.capacity - 1);
+                const uint64_t hi = std::min<uint64_t>(
+                    pos_last, static_cast<uint64_t>(D.pos_base) + D.capacity - 1);
                 const long long len = hi >= lo ? static_cast<long long>(hi - lo + 1) : 0;
-                if (!partial && (lo != t0 || hi != pos))
+                if (!partial && (lo != t0 || hi != pos_last))
                     return fail(JX_ERR_RANGE,
                                 "position %u (window start %llu) is outside the cache rows "
                                 "[%u, %llu); compact or roll back first",
-                                pos, static_cast<unsigned long long>(t0), D.pos_base,
+                                pos_last, static_cast<unsigned long long>(t0), D.pos_base,
                                 static_cast<unsigned long long>(D.pos_base) + D.capacity);
                 PairRow pr{};
                 pr.off = off;
@@ -646,10 +701,14 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 pr.row0 = len > 0 ? static_cast<int>(lo - D.pos_base) : 0;
                 pr.len = static_cast<int>(len);
                 pr.append_row = (!L.shares_kv && pos >= D.pos_base &&
-                                 static_cast<uint64_t>(pos) <
+                                 static_cast<uint64_t>(pos_last) <
                                      static_cast<uint64_t>(D.pos_base) + D.capacity)
                                     ? static_cast<int>(pos - D.pos_base)
                                     : -1;
+                pr.nq = static_cast<int>(nb);
+                pr.io_step = static_cast<int>(n_layers);
+                pr.tok_row0 = static_cast<int>(pos) - static_cast<int>(D.pos_base);
+                pr.window = (L.is_swa && W > 0) ? static_cast<int>(W) : 0;
                 const uint32_t rdim = std::min(L.head_dim, L.rope_dim);
                 pr.rope_half = static_cast<int>(rdim / 2);
                 const float* rf = (neox && !L.is_swa && L.rope_freqs) ? L.rope_freqs : nullptr;
@@ -657,16 +716,20 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 std::memcpy(&base_bits, &L.rope_freq_base, 4);
                 std::memcpy(&yarn_bits, &a->yarn_scale, 4);
                 const uint64_t fh = rf ? hash_floats(rf, rdim / 2) : 0;
+                // nb consecutive rows of the table: positions pos .. pos_last
                 const auto key = std::make_tuple(rdim, base_bits, yarn_bits, pos, fh,
-                                                 static_cast<uint32_t>(L.head_dim));
+                                                 static_cast<uint32_t>(L.head_dim) * 16 + nb);
                 auto itk = rope_ids.find(key);
                 int rid;
                 if (itk == rope_ids.end()) {
-                    rid = static_cast<int>(rope_ids.size());
+                    rid = n_rope_rows;
                     rope_ids.emplace(key, rid);
-                    rope.resize(rope.size() + width);
-                    rope_row(L.head_dim, L.rope_dim, pos, L.rope_freq_base, a->yarn_scale, neox,
-                             rf, rope.data() + static_cast<size_t>(rid) * width, width);
+                    n_rope_rows += static_cast<int>(nb);
+                    rope.resize(static_cast<size_t>(n_rope_rows) * width);
+                    for (uint32_t j = 0; j < nb; ++j)
+                        rope_row(L.head_dim, L.rope_dim, pos + j, L.rope_freq_base, a->yarn_scale,
+                                 neox, rf, rope.data() + static_cast<size_t>(rid + j) * width,
+                                 width);
                 } else {
                     rid = itk->second;
                 }
@@ -682,10 +745,14 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
             for (const PairRow& pr : pairs) {
                 const bool ok = pr.off == o && pr.len >= 0 && pr.row0 >= 0 &&
                                 static_cast<long long>(pr.row0) + pr.len <= D.capacity &&
+                                pr.nq >= 1 && pr.nq <= nq_max &&
                                 (pr.append_row < 0 ||
-                                 (pr.append_row >= pr.row0 && pr.append_row < pr.row0 + pr.len)) &&
-                                pr.rope_row >= 0 && pr.rope_row < static_cast<int>(rope_ids.size()) &&
-                                pr.io >= 0 && pr.io < static_cast<int>(a->n_seqs * n_layers) &&
+                                 (pr.append_row >= pr.row0 &&
+                                  pr.append_row + pr.nq - 1 < pr.row0 + pr.len)) &&
+                                pr.rope_row >= 0 && pr.rope_row + pr.nq - 1 < n_rope_rows &&
+                                pr.io >= 0 &&
+                                pr.io + (pr.nq - 1) * pr.io_step <
+                                    static_cast<int>(a->n_seqs * n_layers) &&
                                 pr.cache_layer >= 0 && pr.cache_layer < static_cast<int>(D.n_layers) &&
                                 pr.seq >= 0 && pr.seq < static_cast<int>(D.n_seqs) &&
                                 pr.rope_half >= 0 && pr.rope_half <= hd / 2;
@@ -695,18 +762,18 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         }
         // ---- launch shape (cached per configuration)
         int stages = 0, cps = 0;
-        const auto skey = std::make_tuple(hd, gp * 16 + kp, kv->opt_stages, kv->opt_ctas_per_sm);
+        const auto skey = std::make_tuple(hd, gp_l * 16 + kp, kv->opt_stages, kv->opt_ctas_per_sm);
         auto sit = kv->shapes.find(skey);
         if (sit != kv->shapes.end()) {
             stages = sit->second.first;
             cps = sit->second.second;
         } else {
-            default_shape(hd, gp, kp, D.dtype, &stages, &cps);
+            default_shape(hd, gp_l, kp, D.dtype, &stages, &cps);
             if (kv->opt_stages) stages = kv->opt_stages;
-            if (decode_smem_bytes(hd, gp, kp, D.dtype, stages) < 0)
+            if (decode_smem_bytes(hd, gp_l, kp, D.dtype, stages) < 0)
                 return fail(JX_ERR_UNSUPPORTED, "no kernel for head_dim %d group %d dtype %d", hd,
                             gp, D.dtype);
-            const int occ = decode_ctas_per_sm(hd, gp, kp, D.dtype, stages);
+            const int occ = decode_ctas_per_sm(hd, gp_l, kp, D.dtype, stages);
             if (occ <= 0)
                 return fail(JX_ERR_UNSUPPORTED, "kernel does not fit with %d stages", stages);
             if (kv->opt_ctas_per_sm) cps = kv->opt_ctas_per_sm;
@@ -717,11 +784,9 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         P = std::min<long long>(P, std::max<long long>(1, (total + 63) / 64));
         if (kv->opt_grid) P = kv->opt_grid;
         if (total == 0) P = 1;
-        // Slice boundaries.  Uniform (CTA c takes rows [c*N/P, (c+1)*N/P)) for
-        // very many segments per CTA (boundary costs average out, and the
-        // balancing pass is linear in segments); otherwise a CTA whose slice
-        // crosses segment boundaries pays for each extra piece (merge, next q)
-        // and gets fewer rows.
+        // Slice boundaries: equal rows plus a cost per piece (merge, next q) --
+        // a CTA whose slice crosses segment boundaries gets fewer rows.  With
+        // the penalty at 0, uniform (CTA c takes rows [c*N/P, (c+1)*N/P)).
         const long long n_kv_segs = static_cast<long long>(pairs.size()) * n_kv;
         std::vector<long long> cta_begin;
         std::vector<int> seg_owner;  // [n_segs][2]: first and last CTA of each segment
@@ -731,7 +796,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                                                                     : (kv->esz == 2 ? 8.0 : 5.0);
         const double penalty_rows =
             penalty_us * split_rows_per_us(kv, static_cast<size_t>(kp) * hd * kv->esz * 2, P);
-        if (penalty_rows > 0.0 && total > 0 && n_kv_segs <= 64 * P) {
+        if (penalty_rows > 0.0 && total > 0) {
             std::vector<long long> seg_off;  // flattened start of each non-empty segment
             seg_off.reserve(static_cast<size_t>(n_kv_segs) + 1);
             for (const PairRow& pr : pairs)
@@ -805,7 +870,7 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 return fail(JX_ERR_CUDA, "append launch failed: %s", cudaGetErrorString(e));
         }
         const long long n_segs = static_cast<long long>(pairs.size()) * n_kv;
-        rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp * kp * (hd + 2),
+        rc = ensure_scratch(kv, static_cast<size_t>(P + n_segs) * gp_l * kp * (hd + 2),
                             static_cast<size_t>(std::max<long long>(n_segs, 1)));
         if (rc) return rc;
 
@@ -850,22 +915,23 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.err = kv->d_err;
         A.n_stages = stages;
         A.n_consumers = consumers_for(stages, kp);
-        A.q_bulk = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
+        A.q_bulk = (!blocks && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0)
+                       ? 1 : 0;  // prefill blocks gather q per token from global memory
         A.skip_append = prefill ? 1 : 0;
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;
         A.scratch_floats = static_cast<long long>(kv->scratch_floats);
         A.n_segments = n_segs;
-        A.n_rope_rows = static_cast<int>(rope_ids.size());
+        A.n_rope_rows = n_rope_rows;
         A.capacity = static_cast<int>(D.capacity);
         A.n_cache_layers = static_cast<int>(D.n_layers);
         A.n_cache_seqs = static_cast<int>(D.n_seqs);
-        A.smem_bytes = decode_smem_bytes(hd, gp, kp, D.dtype, stages);
+        A.smem_bytes = decode_smem_bytes(hd, gp_l, kp, D.dtype, stages);
         A.dbg = kv->d_dbg;
         Lc.tmK = &kv->tmK[box_kind];
         Lc.tmV = &kv->tmV[box_kind];
         Lc.head_dim = hd;
-        Lc.gp = gp;
+        Lc.gp = gp_l;
         Lc.kp = kp;
         Lc.dtype = D.dtype;
         Lc.grid = static_cast<int>(P);
@@ -1298,7 +1364,7 @@ int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream) {
 
 int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
     if (!kv || !key) return fail(JX_ERR_INVALID, "bad option");
-    if (value < 0 && std::strcmp(key, "pdl") != 0)
+    if (value < 0 && std::strcmp(key, "pdl") != 0 && std::strcmp(key, "split_penalty_us") != 0)
         return fail(JX_ERR_INVALID, "option '%s' takes a non-negative value", key);
     if (!std::strcmp(key, "ctas_per_sm")) kv->opt_ctas_per_sm = value;
     else if (!std::strcmp(key, "stages")) {
@@ -1308,7 +1374,7 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
     else if (!std::strcmp(key, "pdl")) kv->opt_pdl = value < 0 ? -1 : (value ? 1 : 0);
     else if (!std::strcmp(key, "timing")) kv->opt_timing = value ? 1 : 0;
     else if (!std::strcmp(key, "split_penalty_us"))
-        kv->opt_split_penalty_us = static_cast<float>(value);
+        kv->opt_split_penalty_us = value < 0 ? -1.0f : static_cast<float>(value);
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;
 }
