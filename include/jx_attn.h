@@ -16,7 +16,10 @@
  *     cudaStream_t; NULL is the legacy default stream).  Calls on one jx_kv
  *     must be ordered on one stream, as forward_token is serialised by
  *     engine_mtx_ (src/transformer.cpp:2361).  Distinct handles are independent.
- *   - q/k/v/out and partial buffers are caller-owned DEVICE pointers; position
+ *   - q/k/v/out and partial buffers are caller-owned pointers to the cache's
+ *     device memory or to pinned (page-locked) host memory -- the kernel then
+ *     reads the inputs and writes the output over PCIe itself, with no copy
+ *     of its own; pageable host memory is refused (JX_ERR_INVALID).  Position
  *     and descriptor arrays are HOST pointers.
  *   - There is no CPU implementation behind this header: without a B200 the
  *     library reports JX_ERR_CUDA.
@@ -96,10 +99,12 @@ typedef struct {
     const int32_t* seq_ids;   /* HOST [n_seqs] cache sequence of each step row, or NULL
                                  for sequences 0..n_seqs-1 */
     const int32_t* pos;       /* HOST [n_seqs] position written this step (slot.seq_pos) */
-    const float* q;           /* DEVICE [n_seqs][n_layers][q_stride] fp32 (not modified) */
-    const float* k;           /* DEVICE [n_seqs][n_layers][kv_stride] fp32 (not modified) */
-    const float* v;           /* DEVICE [n_seqs][n_layers][kv_stride] fp32 */
-    float* out;               /* DEVICE [n_seqs][n_layers][q_stride] fp32 (attn_out) */
+    const float* q;           /* DEVICE or pinned HOST [n_seqs][n_layers][q_stride] fp32
+                                 (not modified) */
+    const float* k;           /* DEVICE or pinned HOST [n_seqs][n_layers][kv_stride] fp32 */
+    const float* v;           /* DEVICE or pinned HOST [n_seqs][n_layers][kv_stride] fp32 */
+    float* out;               /* DEVICE or pinned HOST [n_seqs][n_layers][q_stride] fp32
+                                 (attn_out) */
     uint32_t q_stride;        /* >= n_heads*head_dim (hp.q_dim for the engine's q vector) */
     uint32_t kv_stride;       /* >= n_kv_heads*head_dim */
     float scale;              /* 1/sqrt(head_dim), or 1.0 for gemma4 (transformer.cpp:2525) */

@@ -43,10 +43,15 @@ def _stream_ptr(stream) -> Optional[int]:
     return None
 
 
-def _dev_ptr(t, name: str, min_elems: int) -> int:
+def _dev_ptr(t, name: str, min_elems: int, host_ok: bool = False) -> int:
+    """Address of a contiguous float32 tensor on the device -- or, where
+    host_ok, in pinned host memory (the kernel then reads / writes it over
+    PCIe, with no separate copy)."""
     import torch
-    if not isinstance(t, torch.Tensor) or not t.is_cuda:
-        raise JxError(-1, f"{name} must be a CUDA tensor")
+    if not isinstance(t, torch.Tensor):
+        raise JxError(-1, f"{name} must be a tensor")
+    if not t.is_cuda and not (host_ok and t.device.type == "cpu" and t.is_pinned()):
+        raise JxError(-1, f"{name} must be a CUDA tensor" + (" or pinned host tensor" if host_ok else ""))
     if t.dtype != torch.float32 or not t.is_contiguous():
         raise JxError(-1, f"{name} must be a contiguous float32 tensor")
     if t.numel() < min_elems:
@@ -267,10 +272,10 @@ def _step_args(cache, layers, q, k, v, out, pos, n_heads, n_kv_heads, scale, sof
     a.n_heads, a.n_kv_heads, a.n_seqs = n_heads, n_kv_heads, n
     a.seq_ids = C.cast(sid, C.POINTER(C.c_int32)) if sid is not None else None
     a.pos = C.cast(pos_a, C.POINTER(C.c_int32))
-    a.q = _dev_ptr(q, "q", rows * q_stride)
-    a.k = _dev_ptr(k, "k", rows * kv_stride)
-    a.v = _dev_ptr(v, "v", rows * kv_stride)
-    a.out = _dev_ptr(out, "out", rows * q_stride) if out is not None else None
+    a.q = _dev_ptr(q, "q", rows * q_stride, host_ok=True)
+    a.k = _dev_ptr(k, "k", rows * kv_stride, host_ok=True)
+    a.v = _dev_ptr(v, "v", rows * kv_stride, host_ok=True)
+    a.out = _dev_ptr(out, "out", rows * q_stride, host_ok=True) if out is not None else None
     a.q_stride, a.kv_stride = q_stride, kv_stride
     a.scale, a.softcap = float(scale), float(softcap)
     a.sliding_window, a.yarn_scale, a.rope_neox = int(sliding_window), float(yarn_scale), int(neox)

@@ -533,6 +533,29 @@ std::vector<long long> balanced_split(const std::vector<long long>& seg_off, lon
     return b;
 }
 
+// q/k/v/out (and partials) may live in this device's memory or in pinned
+// (page-locked) host memory, which the kernel reads and writes over PCIe;
+// pageable host memory or another device's memory is refused, since a
+// kernel touching it would fault.  *host tells which.
+int check_step_ptr(const void* p, const char* name, int device, bool* host) {
+    cudaPointerAttributes at{};
+    const cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(JX_ERR_INVALID, "%s: not a CUDA-visible pointer (%s)", name, cudaGetErrorString(e));
+    }
+    if (at.type == cudaMemoryTypeHost) {
+        *host = true;
+        return JX_OK;
+    }
+    *host = false;
+    if ((at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) && at.device == device)
+        return JX_OK;
+    return fail(JX_ERR_INVALID,
+                "%s must be memory of device %d or pinned host memory (pageable host memory "
+                "or another device's memory would fault the kernel)", name, device);
+}
+
 int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
               float* partials, cudaStream_t stream, bool prefill = false) {
     if (!kv || !layers || !a) return fail(JX_ERR_INVALID, "null handle, layers or args");
@@ -556,6 +579,16 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     std::vector<DecodeLaunch> launched;
     const bool partial = partials != nullptr;
     if (!partial && !a->out) return fail(JX_ERR_INVALID, "null out");
+    bool q_host = false;
+    {
+        bool h = false;
+        int rc0 = check_step_ptr(a->q, "q", kv->d.device, &q_host);
+        if (!rc0) rc0 = check_step_ptr(a->k, "k", kv->d.device, &h);
+        if (!rc0) rc0 = check_step_ptr(a->v, "v", kv->d.device, &h);
+        if (!rc0 && a->out) rc0 = check_step_ptr(a->out, "out", kv->d.device, &h);
+        if (!rc0 && partial) rc0 = check_step_ptr(partials, "partials", kv->d.device, &h);
+        if (rc0) return rc0;
+    }
     if (a->n_kv_heads == 0 || a->n_heads == 0 || a->n_heads % a->n_kv_heads != 0)
         return fail(JX_ERR_UNSUPPORTED, "n_heads (%u) must be a multiple of n_kv_heads (%u)",
                     a->n_heads, a->n_kv_heads);
@@ -915,8 +948,10 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.err = kv->d_err;
         A.n_stages = stages;
         A.n_consumers = consumers_for(stages, kp);
-        A.q_bulk = (!blocks && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0)
-                       ? 1 : 0;  // prefill blocks gather q per token from global memory
+        // bulk prefetch of q: device memory, 16-byte rows (prefill blocks and
+        // host-resident q are read with ordinary loads)
+        A.q_bulk = (!blocks && !q_host && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 &&
+                    a->q_stride % 4 == 0) ? 1 : 0;
         A.skip_append = prefill ? 1 : 0;
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;

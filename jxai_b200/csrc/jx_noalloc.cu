@@ -301,7 +301,14 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     A.dbg = reinterpret_cast<int*>(scratch) + 8;
     A.n_stages = stages;
     A.n_consumers = consumers_for(stages, kp);
-    A.q_bulk = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
+    {
+        cudaPointerAttributes at{};
+        const bool q_dev = cudaPointerGetAttributes(&at, a->q) == cudaSuccess &&
+                           at.type == cudaMemoryTypeDevice;
+        cudaGetLastError();
+        A.q_bulk = (q_dev && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0)
+                       ? 1 : 0;
+    }
     A.n_io = static_cast<long long>(n_pairs);
     A.cache_elems = A.seq_stride * D.n_seqs;
     A.scratch_floats = static_cast<long long>(partial_floats);

@@ -194,3 +194,58 @@ def test_step_timer_reports_device_time():
     ms = cache.last_step_ms()
     assert 0.0 < ms < 1000.0
     cache.close()
+
+
+def test_step_on_pinned_host_buffers():
+    # q/k/v/out in pinned host memory: the kernel reads and writes them over PCIe
+    import jxai_b200 as jx
+    torch = _torch()
+    rng = np.random.default_rng(21)
+    H, HK, hd, L, T = 8, 2, 64, 2, 300
+    rs = HK * hd
+    kc = random_cache(rng, (1, L, T, rs), F32)
+    vc = random_cache(rng, (1, L, T, rs), F32)
+    q = rng.standard_normal((1, L, H * hd)).astype(np.float32)
+    k = rng.standard_normal((1, L, rs)).astype(np.float32)
+    v = rng.standard_normal((1, L, rs)).astype(np.float32)
+    layers = [jx.Layer(hd, hd, 5e5, 0), jx.Layer(hd, hd, 1e6, 1)]
+    cache = jx.KVCache(1, L, T, rs, "f32")
+    for l in range(L):
+        cache.write_rows(0, l, 0, 0, kc[0, l])
+        cache.write_rows(0, l, 1, 0, vc[0, l])
+    qh, kh, vh = (torch.from_numpy(x).pin_memory() for x in (q, k, v))
+    oh = torch.full(qh.shape, float("nan")).pin_memory()
+    jx.attn_step(cache, layers, qh, kh, vh, oh, [T - 1], H, HK, neox=False)
+    torch.cuda.synchronize()
+    assert cache.check_device_error() == 0
+    ko, vo = kc.copy(), vc.copy()
+    ref = oracle_step(ko, vo, F32, [T - 1], layers, q, k, v, H, HK, hd, 1 / math.sqrt(hd),
+                      neox=False)
+    assert np.abs(oh.numpy() - ref).max() <= TOL
+    for l in range(L):
+        assert np.array_equal(cache.read_rows(0, l, 0, T - 1, 1)[0], ko[0, l, T - 1])
+    cache.close()
+
+
+def test_pageable_host_pointer_is_refused_before_any_launch():
+    # head_dim 48 is unsupported too: should the pointer check ever let a
+    # pageable buffer through, the call still ends on the host (-4), not in a kernel
+    import ctypes as C
+    import jxai_b200 as jx
+    from jxai_b200 import _lib
+    cache = jx.KVCache(1, 1, 64, 96, "f32")
+    lib = jx.load_library()
+    buf = np.zeros(4096, dtype=np.float32)          # pageable host memory
+    p = buf.ctypes.data
+    layer = _lib.LayerDesc(48, 48, 1e4, 0, 0, 0, None)
+    pos = (C.c_int32 * 1)(10)
+    a = _lib.StepArgs()
+    a.n_heads, a.n_kv_heads, a.n_seqs = 2, 2, 1
+    a.seq_ids, a.pos = None, C.cast(pos, C.POINTER(C.c_int32))
+    a.q = a.k = a.v = a.out = p
+    a.q_stride, a.kv_stride = 96, 96
+    a.scale, a.softcap, a.sliding_window, a.yarn_scale, a.rope_neox = 0.14, 0.0, 0, 1.0, 1
+    rc = lib.jx_attn_step(cache.handle, C.byref(layer), 1, C.byref(a), None)
+    assert rc == _lib.JX_ERR_INVALID, rc
+    assert b"pinned" in lib.jx_last_error_string()
+    cache.close()
