@@ -15,6 +15,11 @@
 //   // after the last layer, as transformer.cpp:2792:
 //   slot.seq_pos++;
 //
+// Two wider forms of the same block: forward_batch runs one layer for several
+// slots at once (one token each, at each slot's seq_pos), and forward_prompt
+// runs one layer for n consecutive prompt tokens of one slot (the prompt loop
+// of transformer.cpp:3092-3095 done layer by layer instead of token by token).
+//
 // Header-only; link with libjxattn.so and the CUDA runtime.  Every call
 // returns a jx status (0 = JX_OK); jx_last_error_string() has the message.
 #ifndef JX_ENGINE_HPP
@@ -50,7 +55,7 @@ class DeviceKVCache {
   public:
     DeviceKVCache(const Hyper& hp, uint32_t max_slots, jx_dtype dtype = JX_F16_TRUNC,
                   int device = 0)
-        : hp_(hp) {
+        : hp_(hp), max_slots_(max_slots) {
         jx_kv_desc d{};
         d.n_seqs = max_slots;
         d.n_layers = hp.n_layers;
@@ -68,9 +73,11 @@ class DeviceKVCache {
     int status() const { return status_; }  // JX_OK when the allocation succeeded
     jx_kv* handle() const { return kv_; }
     const Hyper& hyper() const { return hp_; }
+    uint32_t max_slots() const { return max_slots_; }
 
   private:
     Hyper hp_;
+    uint32_t max_slots_ = 0;
     jx_kv* kv_ = nullptr;
     int status_ = JX_ERR_INVALID;
 };
@@ -143,20 +150,9 @@ class AttentionBlock {
   public:
     explicit AttentionBlock(DeviceKVCache& c, cudaStream_t stream = nullptr)
         : cache_(c), stream_(stream) {
-        const Hyper& hp = c.hyper();
-        status_ = JX_OK;
-        if (cudaMalloc(&d_q_, sizeof(float) * hp.q_dim) != cudaSuccess ||
-            cudaMalloc(&d_k_, sizeof(float) * hp.kv_dim) != cudaSuccess ||
-            cudaMalloc(&d_v_, sizeof(float) * hp.kv_dim) != cudaSuccess ||
-            cudaMalloc(&d_out_, sizeof(float) * hp.q_dim) != cudaSuccess)
-            status_ = JX_ERR_NOMEM;
+        status_ = reserve(1);
     }
-    ~AttentionBlock() {
-        cudaFree(d_q_);
-        cudaFree(d_k_);
-        cudaFree(d_v_);
-        cudaFree(d_out_);
-    }
+    ~AttentionBlock() { release(); }
     AttentionBlock(const AttentionBlock&) = delete;
     AttentionBlock& operator=(const AttentionBlock&) = delete;
 
@@ -172,6 +168,102 @@ class AttentionBlock {
             cudaMemcpyAsync(d_k_, k, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
             cudaMemcpyAsync(d_v_, v, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
             return JX_ERR_CUDA;
+        int32_t seq = static_cast<int32_t>(slot.slot_id), p = static_cast<int32_t>(pos);
+        jx_layer_desc L = desc(lw);
+        jx_step_args a = args(lw, 1, &seq, &p);
+        int rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_);
+        if (rc) return rc;
+        return fetch(attn_out, q_dim * 4);
+    }
+
+    // One layer for n slots at once, one token each at slots[i]->seq_pos (a
+    // serving loop's batched decode in place of one forward_token per request
+    // under engine_mtx_, transformer.cpp:2361).  Host rows: q and attn_out
+    // [n][hp.q_dim], k and v [n][hp.kv_dim]; row i belongs to slots[i].  A slot
+    // appears at most once per call.
+    int forward_batch(KVCacheSlot* const* slots, uint32_t n, const LayerAttn& lw,
+                      const float* q, const float* k, const float* v, float* attn_out) {
+        if (status_) return status_;
+        if (n == 0) return JX_OK;
+        if (!slots) return JX_ERR_INVALID;
+        int rc = reserve(n);
+        if (rc) return rc;
+        seq_.resize(n);
+        pos_.resize(n);
+        for (uint32_t i = 0; i < n; ++i) {
+            if (!slots[i]) return JX_ERR_INVALID;
+            seq_[i] = static_cast<int32_t>(slots[i]->slot_id);
+            pos_[i] = static_cast<int32_t>(slots[i]->seq_pos);
+        }
+        if ((rc = upload(q, k, v, n))) return rc;
+        jx_layer_desc L = desc(lw);
+        jx_step_args a = args(lw, n, seq_.data(), pos_.data());
+        if ((rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_))) return rc;
+        return fetch(attn_out, static_cast<size_t>(n) * cache_.hyper().q_dim * 4);
+    }
+
+    // One layer for n_tokens consecutive prompt tokens of one slot, at
+    // positions pos0, pos0+1, ...: each token's k and v are appended and each
+    // token attends causally over the rows up to its own position, the same
+    // result as feeding the tokens one at a time (transformer.cpp:3092-3095).
+    // Host rows as in forward_batch, one per token.  The caller advances
+    // slot.seq_pos by n_tokens after the last layer.
+    int forward_prompt(KVCacheSlot& slot, const LayerAttn& lw, const float* q, const float* k,
+                       const float* v, float* attn_out, uint32_t n_tokens, uint32_t pos0) {
+        if (status_) return status_;
+        if (n_tokens == 0) return JX_OK;
+        int rc = reserve(n_tokens);
+        if (rc) return rc;
+        seq_.assign(n_tokens, static_cast<int32_t>(slot.slot_id));
+        pos_.resize(n_tokens);
+        for (uint32_t t = 0; t < n_tokens; ++t) pos_[t] = static_cast<int32_t>(pos0 + t);
+        if ((rc = upload(q, k, v, n_tokens))) return rc;
+        jx_layer_desc L = desc(lw);
+        jx_step_args a = args(lw, n_tokens, seq_.data(), pos_.data());
+        if ((rc = jx_attn_prefill(cache_.handle(), &L, 1, &a, stream_))) return rc;
+        return fetch(attn_out, static_cast<size_t>(n_tokens) * cache_.hyper().q_dim * 4);
+    }
+
+  private:
+    // device staging for `rows` rows of q/k/v/out (grown, never shrunk)
+    int reserve(uint32_t rows) {
+        if (rows <= rows_) return JX_OK;
+        release();
+        const Hyper& hp = cache_.hyper();
+        const size_t qb = sizeof(float) * hp.q_dim * rows, kb = sizeof(float) * hp.kv_dim * rows;
+        if (cudaMalloc(&d_q_, qb) != cudaSuccess || cudaMalloc(&d_k_, kb) != cudaSuccess ||
+            cudaMalloc(&d_v_, kb) != cudaSuccess || cudaMalloc(&d_out_, qb) != cudaSuccess) {
+            release();
+            return JX_ERR_NOMEM;
+        }
+        rows_ = rows;
+        return JX_OK;
+    }
+    void release() {
+        cudaFree(d_q_);
+        cudaFree(d_k_);
+        cudaFree(d_v_);
+        cudaFree(d_out_);
+        d_q_ = d_k_ = d_v_ = d_out_ = nullptr;
+        rows_ = 0;
+    }
+    int upload(const float* q, const float* k, const float* v, uint32_t rows) {
+        const Hyper& hp = cache_.hyper();
+        const size_t qb = sizeof(float) * hp.q_dim * rows, kb = sizeof(float) * hp.kv_dim * rows;
+        if (cudaMemcpyAsync(d_q_, q, qb, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(d_k_, k, kb, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(d_v_, v, kb, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+            return JX_ERR_CUDA;
+        return JX_OK;
+    }
+    int fetch(float* attn_out, size_t bytes) {
+        if (cudaMemcpyAsync(attn_out, d_out_, bytes, cudaMemcpyDeviceToHost, stream_) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(stream_) != cudaSuccess)
+            return JX_ERR_CUDA;
+        return JX_OK;
+    }
+    static jx_layer_desc desc(const LayerAttn& lw) {
         jx_layer_desc L{};
         L.head_dim = lw.head_dim;
         L.rope_dim = lw.rope_dim;
@@ -180,13 +272,17 @@ class AttentionBlock {
         L.is_swa = lw.is_swa ? 1 : 0;
         L.shares_kv = lw.shares_kv ? 1 : 0;
         L.rope_freqs = lw.rope_freqs;
-        int32_t seq = static_cast<int32_t>(slot.slot_id), p = static_cast<int32_t>(pos);
+        return L;
+    }
+    jx_step_args args(const LayerAttn& lw, uint32_t n, const int32_t* seq,
+                      const int32_t* pos) const {
+        const Hyper& hp = cache_.hyper();
         jx_step_args a{};
         a.n_heads = hp.n_heads;
         a.n_kv_heads = hp.n_kv_heads;
-        a.n_seqs = 1;
-        a.seq_ids = &seq;
-        a.pos = &p;
+        a.n_seqs = n;
+        a.seq_ids = seq;
+        a.pos = pos;
         a.q = d_q_;
         a.k = d_k_;
         a.v = d_v_;
@@ -198,19 +294,14 @@ class AttentionBlock {
         a.sliding_window = hp.sliding_window;
         a.yarn_scale = hp.yarn_scale;
         a.rope_neox = hp.rope_neox ? 1 : 0;
-        int rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_);
-        if (rc) return rc;
-        if (cudaMemcpyAsync(attn_out, d_out_, q_dim * 4, cudaMemcpyDeviceToHost, stream_) !=
-                cudaSuccess ||
-            cudaStreamSynchronize(stream_) != cudaSuccess)
-            return JX_ERR_CUDA;
-        return JX_OK;
+        return a;
     }
 
-  private:
     DeviceKVCache& cache_;
     cudaStream_t stream_;
     float *d_q_ = nullptr, *d_k_ = nullptr, *d_v_ = nullptr, *d_out_ = nullptr;
+    uint32_t rows_ = 0;
+    std::vector<int32_t> seq_, pos_;
     int status_ = JX_ERR_INVALID;
 };
 

@@ -4,10 +4,12 @@ tests/engine/drop_in_driver.cpp is built with g++ against libjxattn.so and runs
 a token stream through jx::KVCacheSlot + jx::AttentionBlock on host vectors:
 per token the slot compacts on overflow (transformer.cpp:2373-2375), every
 layer runs the attention block (:2497-2567), seq_pos advances (:2792); a prefix
-reuse rolls the slot back (:3071-3089).  The test replays the same script
-through the CPU oracle (fp16-truncated cache, the reference's native type) and
-compares every layer's attn_out, then the final seq_pos and compaction count.
-The compile-only check runs without a GPU.
+reuse rolls the slot back (:3071-3089).  The batched forms run several slots
+per layer call (forward_batch) and a whole prompt per layer call
+(forward_prompt).  The test replays the same script through the CPU oracle,
+one token at a time per slot (fp16-truncated cache, the reference's native
+type), and compares every layer's attn_out, then each slot's final seq_pos and
+compaction count.  The compile-only check runs without a GPU.
 """
 import math
 import os
@@ -53,75 +55,124 @@ def test_engine_header_and_driver_compile():
     _compile(None, syntax_only=True)
 
 
-def _script(rng):
-    """Ops: 50 tokens, prefix reuse back to 30, 60 more tokens (crosses the
-    64-row capacity: one compaction)."""
-    ops = [("tok",)] * 50 + [("lcp", 30)] + [("tok",)] * 60
-    tokens = []
-    for op in ops:
-        if op[0] == "tok":
-            tokens.append((rng.standard_normal((L, H * HD)).astype(np.float32),
-                           rng.standard_normal((L, HK * HD)).astype(np.float32),
-                           rng.standard_normal((L, HK * HD)).astype(np.float32)))
-    return ops, tokens
+def _tok(rng, n=None):
+    """q, k, v for one token (n None) or n rows of one layer-major op."""
+    shape = (L,) if n is None else (L, n)
+    return (rng.standard_normal(shape + (H * HD,)).astype(np.float32),
+            rng.standard_normal(shape + (HK * HD,)).astype(np.float32),
+            rng.standard_normal(shape + (HK * HD,)).astype(np.float32))
 
 
-def _write_script(path, ops, tokens):
+def _write_script(path, n_slots, ops):
+    """ops: ("tok", slot, (q, k, v)) | ("lcp", slot, lcp) |
+    ("batch", [slots], (q, k, v) of [L][m][..]) | ("prompt", slot, (q, k, v) of [L][n][..])"""
     with open(path, "wb") as f:
-        np.array([L, H, HK, HD, CAP, 1, F16T, len(ops)], dtype=np.int32).tofile(f)
+        np.array([L, H, HK, HD, CAP, 1, F16T, n_slots, len(ops)], dtype=np.int32).tofile(f)
         np.array([THETA], dtype=np.float32).tofile(f)
-        it = iter(tokens)
         for op in ops:
-            if op[0] == "lcp":
-                np.array([2, op[1]], dtype=np.int32).tofile(f)
+            kind = op[0]
+            if kind == "lcp":
+                np.array([2, op[1], op[2]], dtype=np.int32).tofile(f)
                 continue
-            q, k, v = next(it)
-            np.array([1], dtype=np.int32).tofile(f)
+            if kind == "tok":
+                np.array([1, op[1]], dtype=np.int32).tofile(f)
+            elif kind == "batch":
+                np.array([3, len(op[1])] + list(op[1]), dtype=np.int32).tofile(f)
+            else:
+                np.array([4, op[1], op[2][0].shape[1]], dtype=np.int32).tofile(f)
+            q, k, v = op[2]
             for l in range(L):
                 q[l].tofile(f)
                 k[l].tofile(f)
                 v[l].tofile(f)
 
 
-@pytest.mark.gpu
-def test_engine_drop_in_matches_oracle_over_a_token_stream():
+def _run_driver(n_slots, ops):
     import jxai_b200 as jx
     jx.load_library()  # builds the library if needed
-    rng = np.random.default_rng(2024)
-    ops, tokens = _script(rng)
     with tempfile.TemporaryDirectory() as td:
         exe = os.path.join(td, "driver")
         _compile(exe)
         script, outp = os.path.join(td, "script.bin"), os.path.join(td, "out.bin")
-        _write_script(script, ops, tokens)
+        _write_script(script, n_slots, ops)
         r = subprocess.run([exe, script, outp], capture_output=True, text=True, timeout=300)
         assert r.returncode == 0, r.stderr
         got = np.fromfile(outp, dtype=np.uint8)
-    n_tok = len(tokens)
-    body = got[: n_tok * L * H * HD * 4].view(np.float32).reshape(n_tok, L, H * HD)
-    seq_pos_dev, compactions_dev = got[n_tok * L * H * HD * 4:].view(np.int32)
+    tail = got[len(got) - 8 * n_slots:].view(np.int32).reshape(n_slots, 2)
+    return got[: len(got) - 8 * n_slots].view(np.float32), tail
 
-    # replay through the oracle
+
+def _replay(n_slots, ops):
+    """The same ops through the oracle, one token at a time per slot, with
+    forward_token's compaction on overflow; returns the attn_out rows in the
+    driver's output order and per-slot (seq_pos, compactions)."""
+    import jxai_b200 as jx
     orc = Oracle("port")
     rs = HK * HD
-    kc = np.zeros((1, L, CAP, rs), dtype=np.uint16)
-    vc = np.zeros((1, L, CAP, rs), dtype=np.uint16)
-    layers = [jx.Layer(HD, HD, THETA, l) for l in range(L)]
-    seq_pos, compactions, t = 0, 0, 0
-    worst = 0.0
+    kc = np.zeros((n_slots, L, CAP, rs), dtype=np.uint16)
+    vc = np.zeros((n_slots, L, CAP, rs), dtype=np.uint16)
+    layers = layer_dicts([jx.Layer(HD, HD, THETA, l) for l in range(L)])
+    seq_pos = [0] * n_slots
+    comp = [0] * n_slots
+    scale = 1 / math.sqrt(HD)
+
+    def one(s, q, k, v):   # q [L][H*HD]: one token of slot s through all layers
+        if seq_pos[s] >= CAP:
+            new = orc.compact(kc[s], vc[s], F16T, seq_pos[s], CAP // 2)
+            comp[s] += int(new != seq_pos[s])
+            seq_pos[s] = new
+        o = orc.step(kc[s:s + 1], vc[s:s + 1], F16T, [seq_pos[s]], layers, q[None], k[None],
+                     v[None], H, HK, HD, scale, neox=True)[0]
+        seq_pos[s] += 1
+        return o             # [L][H*HD]
+
+    chunks = []
     for op in ops:
-        if op[0] == "lcp":
-            seq_pos = min(seq_pos, op[1])
-            continue
-        if seq_pos >= CAP:
-            new = orc.compact(kc[0], vc[0], F16T, seq_pos, CAP // 2)
-            compactions += int(new != seq_pos)
-            seq_pos = new
-        q, k, v = tokens[t]
-        ref = orc.step(kc, vc, F16T, [seq_pos], layer_dicts(layers), q[None], k[None], v[None],
-                       H, HK, HD, 1 / math.sqrt(HD), neox=True)
-        worst = max(worst, float(np.abs(body[t] - ref[0]).max()))
-        seq_pos += 1
-        t += 1
-    assert worst <= TOL, worst
-    assert seq_pos_dev == seq_pos and compactions_dev == compactions == 1
+        kind = op[0]
+        if kind == "lcp":
+            seq_pos[op[1]] = min(seq_pos[op[1]], op[2])
+        elif kind == "tok":
+            chunks.append(one(op[1], *op[2]).reshape(-1))
+        else:
+            slots = op[1] if kind == "batch" else [op[1]] * op[2][0].shape[1]
+            q, k, v = op[2]
+            outs = np.stack([one(s, q[:, i], k[:, i], v[:, i]) for i, s in enumerate(slots)],
+                            axis=1)   # [L][rows][H*HD]
+            chunks.append(outs.reshape(-1))
+    return np.concatenate(chunks), np.array(list(zip(seq_pos, comp)), dtype=np.int32)
+
+
+@pytest.mark.gpu
+def test_engine_drop_in_matches_oracle_over_a_token_stream():
+    # 50 tokens, prefix reuse back to 30, 60 more tokens (crosses the 64-row
+    # capacity: one compaction); slot 1 of 2, so the slot id reaches the library
+    rng = np.random.default_rng(2024)
+    ops = [("tok", 1, _tok(rng)) for _ in range(50)] + [("lcp", 1, 30)]
+    ops += [("tok", 1, _tok(rng)) for _ in range(60)]
+    got, tail = _run_driver(2, ops)
+    ref, ref_tail = _replay(2, ops)
+    assert np.abs(got - ref).max() <= TOL
+    assert (tail == ref_tail).all() and tail[1, 1] == 1
+
+
+@pytest.mark.gpu
+def test_engine_batched_slots_and_prompts_match_oracle():
+    # four slots: prompts of different lengths (forward_prompt), then batched
+    # decode over changing subsets of slots (forward_batch), a rollback, and
+    # enough batched tokens that two slots compact on overflow
+    rng = np.random.default_rng(77)
+    ops = [("prompt", 0, _tok(rng, 21)), ("prompt", 2, _tok(rng, 40)),
+           ("tok", 3, _tok(rng)), ("prompt", 3, _tok(rng, 9))]
+    for i in range(30):
+        ids = [0, 1, 2, 3] if i % 3 else [2, 0]
+        ops.append(("batch", ids, _tok(rng, len(ids))))
+    ops.append(("lcp", 0, 12))
+    ops.append(("prompt", 0, _tok(rng, 6)))
+    for _ in range(8):
+        ops.append(("batch", [3, 2, 1, 0], _tok(rng, 4)))
+    got, tail = _run_driver(4, ops)
+    ref, ref_tail = _replay(4, ops)
+    assert got.shape == ref.shape
+    assert np.abs(got - ref).max() <= TOL
+    assert (tail == ref_tail).all()
+    assert tail[:, 1].sum() >= 1   # at least one slot compacted inside a batch

@@ -125,10 +125,12 @@ def test_head_dim_32_and_group_8():
 
 @pytest.mark.parametrize("dtype", [BF16, F16T])
 @pytest.mark.parametrize("shape", [(8, 8, 64), (16, 8, 64), (16, 2, 64), (8, 8, 32), (6, 3, 64),
-                                   (16, 4, 128), (8, 1, 256), (12, 4, 64)])
+                                   (16, 4, 128), (8, 1, 256), (12, 4, 64), (6, 3, 32),
+                                   (3, 1, 32)])
 def test_16bit_tensor_core_path(dtype, shape):
     # 16-bit caches run QK and PV on the tensor cores, two kv heads per tile row
     # when the heads pair up (head_dim 32/64, even kv heads, unpadded group);
+    # otherwise at head_dim 32 one 64-byte row per tile row (64-byte swizzle);
     # grid=5 splits segments into pieces merged across CTAs
     H, HK, hd = shape
     run_case(dtype, H, HK, hd, [1, 17, 32, 33, 300], grid=5, n_layers=2)

@@ -22,7 +22,7 @@ TOL = 1e-4
 
 @pytest.mark.parametrize("dtype", [F32, BF16, F16T])
 @pytest.mark.parametrize("neox", [True, False])
-@pytest.mark.parametrize("shape", [(8, 2, 64), (4, 1, 128)])
+@pytest.mark.parametrize("shape", [(8, 2, 64), (4, 1, 128), (4, 2, 32)])
 @pytest.mark.parametrize("order", ["shuffled", "sorted"])
 def test_prefill_matches_token_serial_oracle(dtype, neox, shape, order):
     # rows in position order per sequence form blocks of 8/G tokens that share
