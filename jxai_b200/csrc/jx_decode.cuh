@@ -91,15 +91,27 @@ struct SmemLayout {
     static constexpr int o_bytes = kConsumerWarps * GS * HD * 4;
     static constexpr int ml_bytes = kConsumerWarps * GS * 2 * 4;
     static constexpr int lohi_bytes = 2 * GS * 4;       // per-column row limits (prefill blocks)
-    static constexpr int misc_bytes = 16 + 2 * 48;      // flags + two split-piece records
+    static constexpr int misc_bytes = 16 + 2 * 48 + 48;  // flags, two split records, new-row record
     static constexpr int n_extra_bars = 4;              // q full[2], q empty[2]
     static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
     static __host__ __device__ constexpr int bars_offset(int ns) {
         return stages_bytes(ns) + q_bytes + qraw_bytes + rope_bytes + p_bytes + o_bytes +
                ml_bytes + lohi_bytes + misc_bytes;
     }
+    static __host__ __device__ constexpr int bars_end(int ns) {
+        return bars_offset(ns) + (ns * 2 + n_extra_bars) * 8;
+    }
+    // Optional, after the barriers: the raw k and v rows of the two prefetched
+    // pieces (the new row's inputs), when they fit the 227 KB a CTA may have.
+    static constexpr int kvraw_bytes = 2 * 2 * KP * HD * 4;
+    static constexpr int kMaxBytes = 227 * 1024;
+    static __host__ __device__ constexpr int kvraw_offset(int ns) { return (bars_end(ns) + 15) & ~15; }
+    static __host__ __device__ constexpr bool kv_prefetch(int ns) {
+        return kvraw_offset(ns) + kvraw_bytes + 1024 <= kMaxBytes;
+    }
     static __host__ __device__ constexpr int total(int ns) {
-        return bars_offset(ns) + (ns * 2 + n_extra_bars) * 8 + 1024;  // + alignment slack
+        return (kv_prefetch(ns) ? kvraw_offset(ns) + kvraw_bytes : bars_end(ns)) +
+               1024;  // + alignment slack
     }
 };
 
@@ -181,26 +193,56 @@ __device__ __forceinline__ long long owner_cta(long long x, long long total, lon
     return ((x + 1) * P - 1) / total;
 }
 
-// Rotates and stores the k and v slice of kv head `kvh` at row pr.append_row
-// (transformer.cpp:2506-2520), one warp.
-template <int HD, int DT>
-__device__ __forceinline__ void append_slice(const DecodeArgs& a, const PairRow& pr, int kvh,
-                                             int kp, int lane) {
-    const float* kin = a.k_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
-    const float* vin = a.v_in + static_cast<long long>(pr.io) * a.kv_stride + kvh * HD;
-    const long long dst = static_cast<long long>(pr.seq) * a.seq_stride +
-                          static_cast<long long>(pr.cache_layer) * a.layer_stride +
-                          static_cast<long long>(pr.append_row) * a.row_stride + kvh * HD;
-    const float2* cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
-    if (!JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && kvh < a.n_kv * kp, 10, pr.io, kvh, 0)) return;
-    if (!JX_CHECKED(a, dst >= 0 && dst + HD <= a.cache_elems, 11, dst, pr.append_row, pr.seq)) return;
-    if (!JX_CHECKED(a, pr.rope_row >= 0 && pr.rope_row < a.n_rope_rows, 12, pr.rope_row, 0, 0)) return;
+// The step's new row (transformer.cpp:2506-2520) for one kv head: k rotated
+// at the row's position, both converted to the cache type, written to the
+// cache in HBM for later steps and into the landed tile's row `rr` in shared
+// memory for this one.  One warp.  The tile was fetched by TMA without waiting
+// for the global store (a generic-proxy global write would need a proxy fence
+// that drains the CTA's loads in flight); the shared-memory copy is the one
+// this step reads, and the fence before the stage is released orders these
+// generic writes before the stage's next TMA write.
+struct PatchRec {
+    long long dst;     // cache element of the row's first kv head
+    const float* kin;  // raw k of that head (shared memory or global)
+    const float* vin;  // raw v of that head
+    const float2* cs;  // (cos, sin) row
+    int rr;            // row within its tile
+    int rope_half;
+    int pad[2];
+};
+static_assert(sizeof(PatchRec) == 48, "PatchRec layout");
+
+template <int HD, int RW, int DT>
+__device__ __forceinline__ void patch_new_row(const DecodeArgs& a, const PatchRec& pp, int h_local,
+                                              unsigned char* Kt, unsigned char* Vt, int lane) {
+    constexpr int ESZ = DT == DT_F32 ? 4 : 2;
+    const long long dst = pp.dst + static_cast<long long>(h_local) * HD;
+    const float* kin = pp.kin + h_local * HD;
+    const float* vin = pp.vin + h_local * HD;
+    const int rr = pp.rr;
+    if (JX_CHECKED(a, dst >= 0 && dst + HD <= a.cache_elems && rr >= 0 && rr < kTileRows, 11, dst,
+                   rr, h_local)) {
 #pragma unroll 2
-    for (int d = lane; d < HD; d += 32) {
-        const float kr = rope_elem(kin, d, pr.rope_half, cs, a.neox != 0);
-        store_kv<DT>(a.k_cache, dst + d, kr);
-        store_kv<DT>(a.v_cache, dst + d, vin[d]);
+        for (int d = lane; d < HD; d += 32) {
+            const float kr = rope_elem(kin, d, pp.rope_half, pp.cs, a.neox != 0);
+            const float vr = vin[d];
+            store_kv<DT>(a.k_cache, dst + d, kr);
+            store_kv<DT>(a.v_cache, dst + d, vr);
+            const uint32_t off = tile_off<RW, DT>(rr, (h_local * HD + d) * ESZ);
+            if constexpr (DT == DT_F32) {
+                *reinterpret_cast<float*>(Kt + off) = kr;
+                *reinterpret_cast<float*>(Vt + off) = vr;
+            } else if constexpr (DT == DT_BF16) {
+                *reinterpret_cast<uint16_t*>(Kt + off) = f32_to_bf16_ref(kr);
+                *reinterpret_cast<uint16_t*>(Vt + off) = f32_to_bf16_ref(vr);
+            } else {
+                *reinterpret_cast<uint16_t*>(Kt + off) = f32_to_f16_trunc_ref(kr);
+                *reinterpret_cast<uint16_t*>(Vt + off) = f32_to_f16_trunc_ref(vr);
+            }
+        }
     }
+    fence_proxy_async_shared();  // before the stage's next TMA write
+    __syncwarp();
 }
 
 // Writes one merged (g, d) element of a finished segment: normalised output,
@@ -235,7 +277,7 @@ struct SplitRec {
     int early;            // 1: counted in when the piece ended (more pieces followed)
     int nq;               // tokens of a prefill block (1 otherwise)
     int io_step;          // io distance between the block's tokens
-    int pad[2];
+    int c_first, c_last;  // first and last CTA of the segment
 };
 static_assert(sizeof(SplitRec) == 48, "SplitRec layout");
 
@@ -618,11 +660,15 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     float* qraw_s = q_s + L::q_bytes / 4;                                  // [2][GS*HD]
     float2* rope_s = reinterpret_cast<float2*>(qraw_s + L::qraw_bytes / 4);  // [2][HD/2]
     float* p_s = reinterpret_cast<float*>(rope_s) + L::rope_bytes / 4;
+    // raw k and v rows of the new row, [2 q slots][k, v][KP*HD], when they fit
+    const bool kv_pre = L::kv_prefetch(NS);
+    float* kvraw_s = reinterpret_cast<float*>(base + L::kvraw_offset(NS));
     float* o_s = p_s + L::p_bytes / 4;
     float* ml_s = o_s + L::o_bytes / 4;
     int* lohi_s = reinterpret_cast<int*>(ml_s + L::ml_bytes / 4);  // [GS] lo, [GS] hi
     int* misc = lohi_s + 2 * GS;  // [1] abort, [2..3] last flags
     SplitRec* recs = reinterpret_cast<SplitRec*>(misc + 4);     // [2]
+    PatchRec* patch = reinterpret_cast<PatchRec*>(recs + 2);    // the piece's new row
     // full[s] at bars+8s, empty[s] at bars+8(NS+s), q full[2], q empty[2] after them
     const uint32_t bars = base_u32 + L::bars_offset(NS);
     const uint32_t qfull = bars + 8 * (2 * NS);
@@ -634,8 +680,9 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     // The next step may be scheduled onto SMs as this grid frees them; it
     // waits (pdl_wait) for this grid's completion before touching any data.
     pdl_launch_dependents();
-    if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) + L::bars_offset(NS) +
-                               8 * (2 * NS + L::n_extra_bars) <= a.smem_bytes &&
+    if (!JX_CHECKED(a, static_cast<int>(base_u32 - raw_u32) +
+                               (kv_pre ? L::kvraw_offset(NS) + L::kvraw_bytes : L::bars_end(NS)) <=
+                               a.smem_bytes &&
                            a.n_consumers >= kSplit && a.n_consumers <= kConsumerWarps &&
                            a.n_consumers % kSplit == 0 && NS % (a.n_consumers / kSplit) == 0,
                     1, a.smem_bytes, NS, a.n_consumers))
@@ -686,8 +733,16 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                                    pr.row0 + pr.len <= a.capacity,
                             30, it.kvh, pr.cache_layer, pr.row0 + pr.len))
                 break;
-            // this piece's raw q (the segment's query heads) and (cos, sin) row
-            // -> q slot piece % 2, ahead of the consumers that rotate it
+            // The segment's newest row, when this piece holds it: its consumer
+            // warp writes it (cache and landed tile) from the raw k/v rows.
+            bool has_app = false;
+            if (kv_pre && pr.append_row >= 0 && !a.skip_append) {
+                const int al = pr.append_row - pr.row0;
+                has_app = al >= it.r && al < it.r + it.n;
+            }
+            // this piece's raw q (the segment's query heads), (cos, sin) row and,
+            // with the new row, raw k and v -> q slot piece % 2, ahead of the
+            // consumers that use them
             if (a.q_bulk) {
                 const int qs = piece & 1;
                 if (piece >= 2)
@@ -696,10 +751,20 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 if (lane == 0 && *abort_flag == 0 &&
                     JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
                                       pr.rope_row < a.n_rope_rows &&
-                                      (it.kvh + 1) * a.G <= a.n_heads,
+                                      (it.kvh + 1) * a.G <= a.n_heads &&
+                                      (it.kvh + 1) * KP * HD <= a.kv_stride,
                                32, pr.io, pr.rope_row, it.kvh)) {
                     const uint32_t qb = static_cast<uint32_t>(a.G) * HD * 4;
-                    mbar_arrive_expect_tx(qfull + 8 * qs, qb + HD * 4);
+                    constexpr uint32_t kvb = KP * HD * 4;
+                    mbar_arrive_expect_tx(qfull + 8 * qs, qb + HD * 4 + (has_app ? 2 * kvb : 0));
+                    if (has_app) {
+                        const long long kv_off = static_cast<long long>(pr.io) * a.kv_stride +
+                                                 static_cast<long long>(it.kvh) * KP * HD;
+                        bulk_load(smem_u32(kvraw_s + qs * 2 * KP * HD), a.k_in + kv_off, kvb,
+                                  qfull + 8 * qs);
+                        bulk_load(smem_u32(kvraw_s + qs * 2 * KP * HD + KP * HD), a.v_in + kv_off,
+                                  kvb, qfull + 8 * qs);
+                    }
                     bulk_load(smem_u32(qraw_s + qs * GS * HD),
                               a.q + static_cast<long long>(pr.io) * a.q_stride +
                                   static_cast<long long>(it.kvh) * a.G * HD,
@@ -712,26 +777,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 }
                 __syncwarp();
             }
-            // Tile holding the segment's newest row, when this piece holds it; the
-            // row is stored (and fenced) before that tile is loaded.  In the CTA's
-            // first piece -- the kernel's ramp, ring empty -- that is just before
-            // the tile; later pieces find the ring full of the previous piece, so
-            // their append goes first and its latency hides behind those tiles.
-            int t_app = -1;
-            if (pr.append_row >= 0 && !a.skip_append) {
-                const int al = pr.append_row - pr.row0;
-                if (al >= it.r && al < it.r + it.n) t_app = (al - it.r) / kTileRows;
-            }
-            if (piece > 0 && t_app >= 0) t_app = 0;
             ++piece;
             for (int t = 0; t < ntiles; ++t, ++tile) {
-                if (t == t_app) {
-#pragma unroll
-                    for (int kp = 0; kp < KP; ++kp)
-                        append_slice<HD, DT>(a, pr, it.kvh * KP + kp, KP, lane);
-                    fence_proxy_async_global();
-                    __syncwarp();
-                }
                 const int cur_stage = stage;
                 const uint32_t cur_phase = phase;
                 if (++stage == NS) {
@@ -825,12 +872,59 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         const PairRow& pr = it.pr;
         const int kvh = it.kvh;
         const bool blocked = pr.nq > 1;  // a prefill block of several tokens
+        // A piece that is not a whole segment is counted in after it ends,
+        // against the first and last CTA of its segment: read them now, so
+        // that the load is not on the count-in's path.
+        int2 owner = make_int2(0, 0);
+        if (ctid == 0 && !(it.r == 0 && it.n == pr.len)) {
+            const long long sg = static_cast<long long>(it.pi) * a.n_kv + kvh;
+            if (!a.seg_owner) {
+                owner.x = static_cast<int>(owner_cta(it.seg_start, a.total, P));
+                owner.y = static_cast<int>(owner_cta(it.seg_start + pr.len - 1, a.total, P));
+            } else if (sg >= 0 && sg < a.n_segments) {
+                owner = __ldg(reinterpret_cast<const int2*>(a.seg_owner) + sg);
+            }
+        }
+
+        // The segment's newest row, when this piece holds it (index within the
+        // piece): the consumer warp(s) of its tile write it (patch_new_row), and
+        // the piece's q slot, which holds its raw k and v, is released after the
+        // piece's tiles rather than after the q rotation.
+        int app_row = -1;
+        if (pr.append_row >= 0 && !a.skip_append) {
+            const int al = pr.append_row - pr.row0;
+            if (al >= it.r && al < it.r + it.n) app_row = al - it.r;
+        }
+        const int qs_piece = cpiece & 1;
+        const bool slot_kv = a.q_bulk && kv_pre && app_row >= 0;  // inputs in the q slot
+        if (app_row >= 0 && ctid == 0) {
+            // read by the tile's warp(s) after the barrier below; the previous
+            // piece's readers passed the barrier that ended its tiles
+            PatchRec& pp = *patch;
+            pp.dst = static_cast<long long>(pr.seq) * a.seq_stride +
+                     static_cast<long long>(pr.cache_layer) * a.layer_stride +
+                     static_cast<long long>(pr.append_row) * a.row_stride +
+                     static_cast<long long>(kvh) * KP * HD;
+            if (slot_kv) {
+                pp.kin = kvraw_s + qs_piece * 2 * KP * HD;
+                pp.vin = pp.kin + KP * HD;
+                pp.cs = rope_s + qs_piece * (HD / 2);
+            } else {
+                const long long off = static_cast<long long>(pr.io) * a.kv_stride +
+                                      static_cast<long long>(kvh) * KP * HD;
+                pp.kin = a.k_in + off;
+                pp.vin = a.v_in + off;
+                pp.cs = a.rope + static_cast<long long>(pr.rope_row) * (HD / 2);
+            }
+            pp.rr = app_row & (kTileRows - 1);
+            pp.rope_half = pr.rope_half;
+        }
 
         // q rotation for this segment's query group -> q_s (padded heads = 0).
         // Every reader of q_s for the previous piece passed the barrier that
         // ended that piece's tiles.
         if (a.q_bulk) {
-            const int qs = cpiece & 1;
+            const int qs = qs_piece;
             mbar_wait_bounded(qfull + 8 * qs, (cpiece >> 1) & 1, abort_flag, a.err, a.dbg, 5,
                               cpiece);
             const float* qr = qraw_s + qs * GS * HD;
@@ -840,7 +934,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 q_s[idx] = g < a.G ? rope_elem(qr + g * HD, d, pr.rope_half, cs, a.neox != 0) : 0.0f;
             }
             named_bar_sync(1, kConsumerThreads);
-            if (ctid == 0) mbar_arrive(qempty + 8 * qs);
+            if (ctid == 0 && !slot_kv) mbar_arrive(qempty + 8 * qs);
         } else {
         // q straight from global memory; a prefill block's column g is head
         // g % G of token g / G (its own q row and cos/sin row)
@@ -911,8 +1005,10 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             const int t = my_k - tile_base;
             mbar_wait_bounded(bars + 8 * my_stage, my_phase, abort_flag, a.err, a.dbg, 2, my_k);
             const int nvalid = min(kTileRows, it.n - t * kTileRows);
-            const unsigned char* Kt = base + my_stage * 2 * G::TILEB;
-            const unsigned char* Vt = Kt + G::TILEB;
+            unsigned char* Kt = base + my_stage * 2 * G::TILEB;
+            unsigned char* Vt = Kt + G::TILEB;
+            if (app_row >= 0 && t == (app_row >> 5))  // the new row of this warp's kv head
+                patch_new_row<HD, RW, DT>(a, *patch, kSplit > 1 ? warp % kSplit : 0, Kt, Vt, lane);
             if constexpr (kMma) {
                 const uint32_t ku = base_u32 + my_stage * 2 * G::TILEB;
                 mw.tile(ku, base + my_stage * 2 * G::TILEB + G::TILEB, ku + G::TILEB, nvalid,
@@ -1087,6 +1183,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                     o_s[(warp * GS + g) * HD + lane * G::DPL + k] = o[g][k];
         }
         named_bar_sync(1, kConsumerThreads);
+        // every use of the piece's raw k and v precedes the barrier just passed
+        if (slot_kv && ctid == 0) mbar_arrive(qempty + 8 * qs_piece);
 
         const bool whole = it.r == 0 && it.n == pr.len;
         const long long seg = static_cast<long long>(it.pi) * a.n_kv + kvh;
@@ -1132,6 +1230,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                     r.early = early ? 1 : 0;
                     r.nq = blocked ? pr.nq : 1;
                     r.io_step = pr.io_step;
+                    r.c_first = owner.x;
+                    r.c_last = owner.y;
                 }
                 if (early) pending_seg = seg;  // counted in after the next piece's first barrier
                 ++n_split;
@@ -1150,10 +1250,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             bool fence = false;
             for (int k = 0; k < n_split; ++k) {
                 const SplitRec& r = recs[k];
-                const long long c_first = a.seg_owner ? a.seg_owner[2 * r.seg]
-                                                      : owner_cta(r.seg_start, a.total, P);
-                const long long c_last = a.seg_owner ? a.seg_owner[2 * r.seg + 1]
-                                                     : owner_cta(r.seg_start + r.len - 1, a.total, P);
+                const long long c_first = r.c_first, c_last = r.c_last;
                 int last = 0;
                 if (JX_CHECKED(a, r.seg >= 0 && r.seg < a.n_segments &&
                                       c_last + r.seg < P + a.n_segments && c_first >= 0 &&
@@ -1175,11 +1272,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         for (int k = 0; k < n_split; ++k) {
             if (!misc[2 + k]) continue;  // the same for every consumer thread
             const SplitRec r = recs[k];
-            const long long c_first =
-                a.seg_owner ? a.seg_owner[2 * r.seg] : owner_cta(r.seg_start, a.total, P);
-            const long long c_last = a.seg_owner ? a.seg_owner[2 * r.seg + 1]
-                                                 : owner_cta(r.seg_start + r.len - 1, a.total, P);
-            merge_split<HD, GS>(a, r, c_first, c_last, ctid);
+            merge_split<HD, GS>(a, r, r.c_first, r.c_last, ctid);
         }
     }
     (void)JX_CHECKED(a, it.bad == 0, 45 + it.bad, it.x, it.i, b1);

@@ -579,12 +579,12 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     std::vector<DecodeLaunch> launched;
     const bool partial = partials != nullptr;
     if (!partial && !a->out) return fail(JX_ERR_INVALID, "null out");
-    bool q_host = false;
+    bool q_host = false, k_host = false, v_host = false;
     {
         bool h = false;
         int rc0 = check_step_ptr(a->q, "q", kv->d.device, &q_host);
-        if (!rc0) rc0 = check_step_ptr(a->k, "k", kv->d.device, &h);
-        if (!rc0) rc0 = check_step_ptr(a->v, "v", kv->d.device, &h);
+        if (!rc0) rc0 = check_step_ptr(a->k, "k", kv->d.device, &k_host);
+        if (!rc0) rc0 = check_step_ptr(a->v, "v", kv->d.device, &v_host);
         if (!rc0 && a->out) rc0 = check_step_ptr(a->out, "out", kv->d.device, &h);
         if (!rc0 && partial) rc0 = check_step_ptr(partials, "partials", kv->d.device, &h);
         if (rc0) return rc0;
@@ -948,10 +948,14 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         A.err = kv->d_err;
         A.n_stages = stages;
         A.n_consumers = consumers_for(stages, kp);
-        // bulk prefetch of q: device memory, 16-byte rows (prefill blocks and
-        // host-resident q are read with ordinary loads)
-        A.q_bulk = (!blocks && !q_host && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 &&
-                    a->q_stride % 4 == 0) ? 1 : 0;
+        // bulk prefetch of q (and of the k/v rows the step appends): device
+        // memory, 16-byte rows (prefill blocks and host-resident inputs are
+        // read with ordinary loads)
+        A.q_bulk = (!blocks && !q_host && !k_host && !v_host &&
+                    reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(a->k) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(a->v) % 16 == 0 && a->kv_stride % 4 == 0)
+                       ? 1 : 0;
         A.skip_append = prefill ? 1 : 0;
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;

@@ -302,11 +302,19 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     A.n_stages = stages;
     A.n_consumers = consumers_for(stages, kp);
     {
-        cudaPointerAttributes at{};
-        const bool q_dev = cudaPointerGetAttributes(&at, a->q) == cudaSuccess &&
-                           at.type == cudaMemoryTypeDevice;
-        cudaGetLastError();
-        A.q_bulk = (q_dev && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0)
+        // q and the appended k/v rows are bulk-prefetched from device memory
+        // with 16-byte rows; otherwise they are read with ordinary loads
+        auto on_device = [](const void* p) {
+            cudaPointerAttributes at{};
+            const bool dev = cudaPointerGetAttributes(&at, p) == cudaSuccess &&
+                             at.type == cudaMemoryTypeDevice;
+            cudaGetLastError();
+            return dev;
+        };
+        A.q_bulk = (on_device(a->q) && on_device(a->k) && on_device(a->v) &&
+                    reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0 &&
+                    reinterpret_cast<uintptr_t>(a->k) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(a->v) % 16 == 0 && a->kv_stride % 4 == 0)
                        ? 1 : 0;
     }
     A.n_io = static_cast<long long>(n_pairs);
