@@ -15,7 +15,8 @@
 //  * Pipeline.  Warp 4 is the producer: it streams 32-row K and V tiles of the
 //    current piece into a ring of shared-memory stages with 4-D TMA tile loads
 //    (128-byte swizzle, no multicast), completion tracked by mbarriers, and
-//    bulk-copies each piece's q and RoPE row into one of two q slots.
+//    bulk-copies each piece's q and RoPE row (and the raw k/v rows the piece
+//    appends) into one of two q slots.
 //    Warps 0-3 are consumers; tile k goes to stream k % S (S = consumer warps /
 //    warps per tile) with the ring size a multiple of S, so every use of a
 //    given stage is consumed by the same warps, in order.  (A stage whose
@@ -41,9 +42,12 @@
 //    itself in on the segment's counter (no waiting); the CTA that counts in
 //    last merges all partials by log-sum-exp after its own last piece and
 //    resets the counter.
-//  * Append.  The CTA that owns a segment's newest row rotates and stores that
-//    row's k and v slice (producer warp), fences the generic->async proxy, and
-//    only then loads the tile holding it.
+//  * Append.  The consumer warp whose tile holds a segment's newest row
+//    rotates k, converts both rows to the cache type, and stores them to the
+//    cache (for later steps) and into the landed tile (for this one); the raw
+//    rows come with the piece's q in the prefetch.  The tile's load does not
+//    wait for the global store, so no generic->async proxy fence on global
+//    memory holds the ring back.
 //
 // Template parameters: HD = head_dim, GP = query heads per kv head rounded up
 // to 1/2/4/8, DT = cache element type (DT_F32 / DT_BF16 / DT_F16T), KP = kv

@@ -163,12 +163,6 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// Orders this thread's generic-proxy global writes before later async-proxy
-// (TMA) reads of the same bytes.
-__device__ __forceinline__ void fence_proxy_async_global() {
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Orders this thread's generic-proxy shared-memory accesses before later
 // async-proxy (TMA) writes of the same bytes.
 __device__ __forceinline__ void fence_proxy_async_shared() {
