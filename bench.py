@@ -350,8 +350,8 @@ def run_ours(args, rank, world, local_rank):
         # q, k, v and the output in pinned host memory.  Sharded-position
         # steps (a collective) stage them: one H2D copy of q|k|v and one D2H
         # copy of the output per step.  Otherwise the C ABI call takes the host
-        # buffers themselves and the kernel reads q/k/v and writes attn_out
-        # over PCIe -- the same bytes cross every step, with no copy launches.
+        # buffers themselves: the library copies q/k/v into device memory with
+        # one staging kernel and the decode kernel writes attn_out over PCIe.
         nq, nk = r.q.numel(), r.k.numel()
         inh = torch.empty(nq + 2 * nk, pin_memory=True)
         inh[:nq].copy_(r.q.reshape(-1).cpu())
@@ -399,7 +399,8 @@ def run_ours(args, rank, world, local_rank):
                "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h),
                "path": ("pinned host q|k|v and attn_out passed to jx_attn_step (C ABI); the "
-                        "kernel reads and writes them over PCIe" if zero_copy else
+                        "library copies q|k|v to device memory with one staging kernel and "
+                        "the decode kernel writes attn_out over PCIe" if zero_copy else
                         "pinned host q|k|v -> one H2D -> jx_attn_step (C ABI) -> one D2H attn_out")}
 
     # ---- CPU baseline (rank 0, N=1)

@@ -157,6 +157,32 @@ __global__ void append_rows_kernel(const PairRow* __restrict__ pairs, int n_pair
     }
 }
 
+// Copies up to three host-resident (pinned) input buffers into device memory
+// at the start of a step: many threads in flight, each input byte crossing
+// PCIe once.  It lets the step's decode launch be scheduled at once
+// (programmatic dependent launch); that launch waits for this grid before it
+// reads the copies.
+__global__ void stage_inputs_kernel(const float* s0, float* d0, long long n0, const float* s1,
+                                    float* d1, long long n1, const float* s2, float* d2,
+                                    long long n2) {
+    pdl_launch_dependents();
+    const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long nthr = static_cast<long long>(gridDim.x) * blockDim.x;
+    const float* src[3] = {s0, s1, s2};
+    float* dst[3] = {d0, d1, d2};
+    const long long n[3] = {n0, n1, n2};
+    for (int b = 0; b < 3; ++b) {
+        if (!src[b] || n[b] <= 0) continue;
+        const bool vec = (reinterpret_cast<uintptr_t>(src[b]) | reinterpret_cast<uintptr_t>(dst[b])) %
+                             16 == 0;
+        const long long n4 = vec ? n[b] / 4 : 0;
+        const float4* s4 = reinterpret_cast<const float4*>(src[b]);
+        float4* d4 = reinterpret_cast<float4*>(dst[b]);
+        for (long long i = tid; i < n4; i += nthr) d4[i] = s4[i];
+        for (long long i = 4 * n4 + tid; i < n[b]; i += nthr) dst[b][i] = src[b][i];
+    }
+}
+
 // Consumer warps for a ring of `stages` when `split` warps share each tile:
 // every stage must be consumed by one group of warps only, so the number of
 // tile streams (warps / split) divides the ring size.
@@ -319,6 +345,9 @@ struct jx_kv {
     float* d_part = nullptr;
     float* d_gather = nullptr;
     size_t part_floats = 0, gather_floats = 0;
+    // device copies of a step's host-resident q/k/v (stage_host_inputs)
+    float* d_stage = nullptr;
+    size_t stage_floats = 0;
 };
 
 namespace {
@@ -1087,18 +1116,82 @@ namespace {
 // device time of everything the step queued (plan upload when it changed,
 // launches) -- the counterpart of forward_token's attention_ms
 // (transformer.cpp:2499, 2567).
+// Host-resident (pinned) q, k and v are copied into device memory by one
+// small kernel at the start of the step, and the step then reads the copies:
+// read in place over PCIe, every CTA that shares a segment fetched the same
+// q rows, and each piece's q (and the new row's k, v) stalled its consumers
+// for a PCIe round trip.  *staged receives the arguments to use (unchanged
+// when nothing is host-resident).  The copies cover exactly the rows the
+// step reads: [rows - 1] strides plus the last row.
+int stage_host_inputs(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+                      const jx_step_args* a, cudaStream_t stream, jx_step_args* staged) {
+    *staged = *a;
+    if (!a->q || !a->k || !a->v || n_layers == 0 || a->n_seqs == 0) return JX_OK;
+    // arguments step_impl would refuse are left to it: nothing is read here
+    if (a->n_kv_heads == 0 || a->n_heads == 0 || a->n_heads % a->n_kv_heads != 0) return JX_OK;
+    for (uint32_t l = 0; l < n_layers; ++l) {
+        const uint32_t hd = layers[l].head_dim;
+        if ((hd != 32 && hd != 64 && hd != 128 && hd != 256) ||
+            a->q_stride < static_cast<uint64_t>(a->n_heads) * hd ||
+            a->kv_stride < static_cast<uint64_t>(a->n_kv_heads) * hd)
+            return JX_OK;
+    }
+    bool host[3] = {false, false, false};
+    const void* ptr[3] = {a->q, a->k, a->v};
+    for (int b = 0; b < 3; ++b) {
+        // queried on every call: a buffer freed and replaced at the same
+        // address may no longer be pinned
+        cudaPointerAttributes at{};
+        if (cudaPointerGetAttributes(&at, ptr[b]) != cudaSuccess) {
+            cudaGetLastError();
+            return JX_OK;  // step_impl reports the bad pointer
+        }
+        host[b] = at.type == cudaMemoryTypeHost;
+    }
+    if (!host[0] && !host[1] && !host[2]) return JX_OK;
+    const long long rows = static_cast<long long>(a->n_seqs) * n_layers;
+    const long long hd_last = layers[n_layers - 1].head_dim;
+    const long long n_q = (rows - 1) * a->q_stride + static_cast<long long>(a->n_heads) * hd_last;
+    const long long n_kv = (rows - 1) * a->kv_stride + static_cast<long long>(a->n_kv_heads) * hd_last;
+    if (n_q <= 0 || n_kv <= 0) return JX_OK;  // step_impl reports the bad shape
+    const long long off_k = (n_q + 3) & ~3ll, off_v = off_k + ((n_kv + 3) & ~3ll);
+    float* before = kv->d_stage;
+    int rc = grow(&kv->d_stage, &kv->stage_floats, static_cast<size_t>(off_v + n_kv));
+    if (rc) return rc;
+    if (kv->d_stage != before) ++kv->generation;  // recorded launches name the old copy
+    const float* src[3] = {host[0] ? a->q : nullptr, host[1] ? a->k : nullptr,
+                           host[2] ? a->v : nullptr};
+    float* dst[3] = {kv->d_stage, kv->d_stage + off_k, kv->d_stage + off_v};
+    const long long work = (host[0] ? n_q : 0) + (host[1] ? 2 * n_kv : 0);
+    const int grid = static_cast<int>(std::min<long long>(
+        std::max<long long>((work / 4 + 255) / 256, 1), 4ll * std::max(kv->num_sms, 1)));
+    stage_inputs_kernel<<<grid, 256, 0, stream>>>(src[0], dst[0], n_q, src[1], dst[1], n_kv,
+                                                  src[2], dst[2], n_kv);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(JX_ERR_CUDA, "input staging launch: %s", cudaGetErrorString(e));
+    if (host[0]) staged->q = dst[0];
+    if (host[1]) staged->k = dst[1];
+    if (host[2]) staged->v = dst[2];
+    return JX_OK;
+}
+
 int timed_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
                float* partials, cudaStream_t stream, bool prefill = false) {
-    if (!kv || !kv->opt_timing)
-        return step_impl(kv, layers, n_layers, a, partials, stream, prefill);
+    if (!kv || !layers || !a) return step_impl(kv, layers, n_layers, a, partials, stream, prefill);
     DeviceGuard guard(kv->d.device);
     if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
-    if (!kv->ev_t0) JX_CUDA(cudaEventCreate(&kv->ev_t0));
-    if (!kv->ev_t1) JX_CUDA(cudaEventCreate(&kv->ev_t1));
-    JX_CUDA(cudaEventRecord(kv->ev_t0, stream));
-    const int rc = step_impl(kv, layers, n_layers, a, partials, stream, prefill);
-    JX_CUDA(cudaEventRecord(kv->ev_t1, stream));
-    kv->timed = rc == JX_OK;
+    if (kv->opt_timing) {
+        if (!kv->ev_t0) JX_CUDA(cudaEventCreate(&kv->ev_t0));
+        if (!kv->ev_t1) JX_CUDA(cudaEventCreate(&kv->ev_t1));
+        JX_CUDA(cudaEventRecord(kv->ev_t0, stream));
+    }
+    jx_step_args staged{};
+    int rc = stage_host_inputs(kv, layers, n_layers, a, stream, &staged);
+    if (!rc) rc = step_impl(kv, layers, n_layers, &staged, partials, stream, prefill);
+    if (kv->opt_timing) {
+        JX_CUDA(cudaEventRecord(kv->ev_t1, stream));
+        kv->timed = rc == JX_OK;
+    }
     return rc;
 }
 
@@ -1176,6 +1269,7 @@ int jx_kv_destroy(jx_kv* kv) {
     cudaFree(kv->d_counters);
     cudaFree(kv->d_part);
     cudaFree(kv->d_gather);
+    cudaFree(kv->d_stage);
     if (kv->ev_t0) cudaEventDestroy(kv->ev_t0);
     if (kv->ev_t1) cudaEventDestroy(kv->ev_t1);
     for (PlanSlot& s : kv->slots) {
