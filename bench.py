@@ -441,9 +441,24 @@ def run_ours(args, rank, world, local_rank):
 
 # ----------------------------------------------------------------------------- CPU side
 
-def _cpu_oracle():
-    """(Oracle, kind): the reference build when present, else the C restatement."""
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0)) or 1
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def _cpu_oracle(all_threads: bool = False):
+    """(Oracle, kind): the reference build when present, else the C restatement.
+
+    all_threads: use every host thread this process may run on, even where a
+    launcher (torchrun sets OMP_NUM_THREADS=1 per rank) asked for fewer -- the
+    reference arm's rank 0 is the only rank that works.
+    """
+    if all_threads:
+        os.environ["OMP_NUM_THREADS"] = str(_host_threads())
+    else:
+        os.environ.setdefault("OMP_NUM_THREADS", str(_host_threads()))
     from oracle.oracle import Oracle, ref_available
     if ref_available():
         return Oracle("ref"), "reference"
@@ -510,7 +525,7 @@ def run_reference(args, rank, world):
     w = W.make(args.config, args.dtype)
     if args.seqs > 0:
         w.lengths = w.lengths[:args.seqs]
-    orc, kind = _cpu_oracle()
+    orc, kind = _cpu_oracle(all_threads=True)
     n_seqs, n_layers, kv_bytes = _cpu_sample_shape(w)
     rng = np.random.default_rng(W.SEED)
     dt, kc, vc, q, k, v, layers, pos, lengths = _cpu_case(w, n_seqs, n_layers, rng)
