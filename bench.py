@@ -54,6 +54,8 @@ def parse_args():
                    help="keep only the first N sequences of the workload (small profiling cases)")
     p.add_argument("--no-graph", action="store_true",
                    help="time K eager launches instead of one CUDA graph of K launches")
+    p.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
+                   help="library option (jx_kv_set_option) for the run's cache; repeatable")
     return p.parse_args()
 
 
@@ -148,7 +150,7 @@ class ClockSampler:
 class Runner:
     """One rank's share of a workload, driven through the public Python API."""
 
-    def __init__(self, w: W.Workload, rank: int, world: int, device: int):
+    def __init__(self, w: W.Workload, rank: int, world: int, device: int, options=()):
         import torch
         import jxai_b200 as jx
         self.torch, self.jx, self.w = torch, jx, w
@@ -170,6 +172,9 @@ class Runner:
         n = len(self.local)
         self.n = n
         self.cache = jx.KVCache(n, w.n_layers, cap, w.kv_dim, w.dtype, device, self.pos_base)
+        for opt in options:
+            key, _, val = opt.partition("=")
+            self.cache.set_option(key, int(val))
         self.cache.fill_normal(rows, W.SEED + rank)
         dev = torch.device("cuda", device)
         self.q = torch.empty(n, w.n_layers, w.q_dim, device=dev)
@@ -239,7 +244,7 @@ def run_ours(args, rank, world, local_rank):
     w = W.make(args.config, args.dtype)
     if args.seqs > 0:
         w.lengths = w.lengths[:args.seqs]
-    r = Runner(w, rank, world, local_rank)
+    r = Runner(w, rank, world, local_rank, args.set)
     stream = torch.cuda.current_stream()
 
     def barrier():
