@@ -56,6 +56,11 @@ def parse_args():
                    help="time K eager launches instead of one CUDA graph of K launches")
     p.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
                    help="library option (jx_kv_set_option) for the run's cache; repeatable")
+    p.add_argument("--engine", action="store_true",
+                   help="per-token latency through the C++ engine drop-in (include/jx_engine.hpp):\n"
+                        "one synchronous block call per layer on host vectors, as forward_token\n"
+                        "makes it; single-sequence full-attention configs (c1, c2, c4)")
+    p.add_argument("--tokens", type=int, default=200, help="timed tokens of --engine")
     return p.parse_args()
 
 
@@ -392,8 +397,10 @@ def run_ours(args, rank, world, local_rank):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
+        h0 = time.perf_counter()
         for _ in range(K):
             e2e_step()
+        host_ms = (time.perf_counter() - h0) * 1e3 / K
         b.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -403,6 +410,7 @@ def run_ours(args, rank, world, local_rank):
         e2e = {"value": round(total_kv * K / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h),
+               "host_issue_ms_per_step": round(host_ms, 5),
                "path": ("pinned host q|k|v and attn_out passed to jx_attn_step (C ABI); the "
                         "library copies q|k|v to device memory with one staging kernel and "
                         "the decode kernel writes attn_out over PCIe" if zero_copy else
@@ -573,6 +581,71 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def _engine_driver() -> str:
+    """tests/engine/engine_latency.cpp built against the in-tree library."""
+    import shutil
+    from jxai_b200 import load_library
+    load_library()  # builds libjxattn.so when it is missing or stale
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    lib_dir = os.path.join(ROOT, "jxai_b200")
+    src = os.path.join(ROOT, "tests", "engine", "engine_latency.cpp")
+    exe = os.path.join(lib_dir, "_build", "engine_latency")
+    os.makedirs(os.path.dirname(exe), exist_ok=True)
+    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-I", os.path.join(ROOT, "include"),
+           "-I", os.path.join(cuda, "include"), src, "-o", exe, "-L", lib_dir, "-ljxattn",
+           "-L", os.path.join(cuda, "lib64"), "-lcudart", f"-Wl,-rpath,{lib_dir}",
+           f"-Wl,-rpath,{os.path.join(cuda, 'lib64')}"]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    return exe
+
+
+def run_engine(args, rank, world):
+    """Per-token attention latency through the C++ engine drop-in.
+
+    forward_token (src/transformer.cpp:2497-2567) runs the block once per
+    layer between CPU matmuls, so every layer is a synchronous round trip:
+    host q/k/v in, attn_out back.  The driver times whole tokens (all layers)
+    with a wall clock, as the reference's attention_ms does (:2499, 2567), for
+    both staging modes of jx::AttentionBlock; the reference's own CPU block is
+    timed beside it on the same shape.
+    """
+    if rank != 0:
+        return
+    w = W.make(args.config, args.dtype)
+    if len(w.lengths) != 1 or w.window:
+        raise SystemExit("--engine runs the single-sequence full-attention configs (c1, c2, c4)")
+    exe = _engine_driver()
+    dt = {"f32": 0, "bf16": 1, "f16": 2}[w.dtype]
+    T = w.lengths[0]
+    res = {}
+    for mode in ("pinned", "copies"):
+        cmd = [exe, str(dt), str(T), str(w.n_layers), str(w.n_heads), str(w.n_kv_heads),
+               str(w.head_dim), str(int(w.neox)), repr(float(w.layers[0].rope_base)),
+               str(args.tokens), str(max(3, args.warmup)), mode]
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+        if r.returncode != 0:
+            raise RuntimeError(f"engine driver failed ({mode}): {r.stderr.strip()}")
+        res[mode] = json.loads(r.stdout.strip().splitlines()[-1])
+    cpu = None
+    if not args.no_cpu_baseline:
+        c = cpu_baseline(w, args.cpu_sample_s)
+        # the CPU sample's KV GB/s over a whole token's KV bytes: its attention_ms
+        c["value"] = round(w.kv_read_bytes() / (c["value"] * 1e9) * 1e3, 4)
+        c["unit"] = "ms per token"
+        cpu = c
+    best = min(res.values(), key=lambda d: d["ms_per_token"])
+    line = {
+        "metric": "engine attention ms per token", "value": best["ms_per_token"], "unit": "ms",
+        "n_gpus": 1, "tokens": args.tokens, "higher_is_better": False, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": dict(w.describe(), path="jx::AttentionBlock::forward once per layer on host "
+                       "vectors, synchronised per layer (forward_token's call pattern)"),
+        "staging": res, "cpu_baseline": cpu,
+        "kv_gbs": round(w.kv_read_bytes() / (best["ms_per_token"] * 1e-3) / 1e9, 2),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -580,6 +653,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.engine:
+        run_engine(args, rank, world)
         return
     import torch
     import torch.distributed as dist

@@ -9,7 +9,7 @@
 //
 //   jx::DeviceKVCache cache(hp, max_slots);            // KVCacheSlot::init for all slots
 //   jx::KVCacheSlot& slot = ...; slot.init(id, cache);
-//   jx::AttentionBlock attn(cache);                     // device staging buffers
+//   jx::AttentionBlock attn(cache);                     // pinned staging buffers
 //   // per layer, in place of transformer.cpp:2497-2567:
 //   attn.forward(slot, layer_desc, q.data(), k.data(), v.data(), attn_out.data(), pos);
 //   // after the last layer, as transformer.cpp:2792:
@@ -29,6 +29,7 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <vector>
 
 #include "jx_attn.h"
@@ -141,6 +142,19 @@ struct LayerAttn {
     const float* rope_freqs = nullptr;  // host, rope_dim/2 factors (Neox, global layers)
 };
 
+// How the block's host rows cross PCIe.
+enum class Staging {
+    // The CPU copies q/k/v into pinned host buffers the library reads directly
+    // (one staging kernel brings them into device memory, chained to the
+    // decode launch) and the decode kernel writes attn_out into a pinned
+    // buffer, which the CPU copies out after the stream synchronises: no
+    // copy-engine transfers on the per-layer critical path.
+    PinnedHost,
+    // cudaMemcpyAsync of q, k and v from the engine's (pageable) vectors into
+    // device buffers, and of attn_out back.
+    DeviceCopies,
+};
+
 // transformer.cpp:2497-2567 for one layer of one slot, host vectors in and
 // out: q (n_heads*head_dim) and k, v (n_kv_heads*head_dim) go up, attn_out
 // (n_heads*head_dim) comes down.  As in the reference, q and k are the
@@ -148,8 +162,9 @@ struct LayerAttn {
 // host q and k are left unrotated (nothing reads them afterwards).
 class AttentionBlock {
   public:
-    explicit AttentionBlock(DeviceKVCache& c, cudaStream_t stream = nullptr)
-        : cache_(c), stream_(stream) {
+    explicit AttentionBlock(DeviceKVCache& c, cudaStream_t stream = nullptr,
+                            Staging staging = Staging::PinnedHost)
+        : cache_(c), stream_(stream), staging_(staging) {
         status_ = reserve(1);
     }
     ~AttentionBlock() { release(); }
@@ -164,14 +179,12 @@ class AttentionBlock {
         const Hyper& hp = cache_.hyper();
         const size_t q_dim = static_cast<size_t>(hp.n_heads) * lw.head_dim;
         const size_t kv_dim = static_cast<size_t>(hp.n_kv_heads) * lw.head_dim;
-        if (cudaMemcpyAsync(d_q_, q, q_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
-            cudaMemcpyAsync(d_k_, k, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
-            cudaMemcpyAsync(d_v_, v, kv_dim * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
-            return JX_ERR_CUDA;
+        int rc = put_rows(q, q_dim, k, v, kv_dim);
+        if (rc) return rc;
         int32_t seq = static_cast<int32_t>(slot.slot_id), p = static_cast<int32_t>(pos);
         jx_layer_desc L = desc(lw);
         jx_step_args a = args(lw, 1, &seq, &p);
-        int rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_);
+        rc = jx_attn_step(cache_.handle(), &L, 1, &a, stream_);
         if (rc) return rc;
         return fetch(attn_out, q_dim * 4);
     }
@@ -225,39 +238,69 @@ class AttentionBlock {
     }
 
   private:
-    // device staging for `rows` rows of q/k/v/out (grown, never shrunk)
+    // staging for `rows` rows of q/k/v/out (grown, never shrunk): pinned host
+    // buffers or device buffers, by the staging mode
     int reserve(uint32_t rows) {
         if (rows <= rows_) return JX_OK;
         release();
         const Hyper& hp = cache_.hyper();
         const size_t qb = sizeof(float) * hp.q_dim * rows, kb = sizeof(float) * hp.kv_dim * rows;
-        if (cudaMalloc(&d_q_, qb) != cudaSuccess || cudaMalloc(&d_k_, kb) != cudaSuccess ||
-            cudaMalloc(&d_v_, kb) != cudaSuccess || cudaMalloc(&d_out_, qb) != cudaSuccess) {
-            release();
-            return JX_ERR_NOMEM;
+        void* p[4] = {nullptr, nullptr, nullptr, nullptr};
+        const size_t sz[4] = {qb, kb, kb, qb};
+        for (int i = 0; i < 4; ++i) {
+            const cudaError_t e = staging_ == Staging::PinnedHost
+                                      ? cudaHostAlloc(&p[i], sz[i], cudaHostAllocDefault)
+                                      : cudaMalloc(&p[i], sz[i]);
+            if (e != cudaSuccess) {
+                for (int j = 0; j < i; ++j) free_buf(p[j]);
+                return JX_ERR_NOMEM;
+            }
         }
+        q_ = static_cast<float*>(p[0]);
+        k_ = static_cast<float*>(p[1]);
+        v_ = static_cast<float*>(p[2]);
+        out_ = static_cast<float*>(p[3]);
         rows_ = rows;
         return JX_OK;
     }
+    void free_buf(void* p) {
+        if (staging_ == Staging::PinnedHost) cudaFreeHost(p);
+        else cudaFree(p);
+    }
     void release() {
-        cudaFree(d_q_);
-        cudaFree(d_k_);
-        cudaFree(d_v_);
-        cudaFree(d_out_);
-        d_q_ = d_k_ = d_v_ = d_out_ = nullptr;
+        free_buf(q_);
+        free_buf(k_);
+        free_buf(v_);
+        free_buf(out_);
+        q_ = k_ = v_ = out_ = nullptr;
         rows_ = 0;
     }
-    int upload(const float* q, const float* k, const float* v, uint32_t rows) {
-        const Hyper& hp = cache_.hyper();
-        const size_t qb = sizeof(float) * hp.q_dim * rows, kb = sizeof(float) * hp.kv_dim * rows;
-        if (cudaMemcpyAsync(d_q_, q, qb, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
-            cudaMemcpyAsync(d_k_, k, kb, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
-            cudaMemcpyAsync(d_v_, v, kb, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+    // one row of q (q_n floats) and of k, v (kv_n floats)
+    int put_rows(const float* q, size_t q_n, const float* k, const float* v, size_t kv_n) {
+        if (staging_ == Staging::PinnedHost) {
+            std::memcpy(q_, q, q_n * 4);
+            std::memcpy(k_, k, kv_n * 4);
+            std::memcpy(v_, v, kv_n * 4);
+            return JX_OK;
+        }
+        if (cudaMemcpyAsync(q_, q, q_n * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(k_, k, kv_n * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess ||
+            cudaMemcpyAsync(v_, v, kv_n * 4, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
             return JX_ERR_CUDA;
         return JX_OK;
     }
+    int upload(const float* q, const float* k, const float* v, uint32_t rows) {
+        const Hyper& hp = cache_.hyper();
+        return put_rows(q, static_cast<size_t>(hp.q_dim) * rows, k, v,
+                        static_cast<size_t>(hp.kv_dim) * rows);
+    }
     int fetch(float* attn_out, size_t bytes) {
-        if (cudaMemcpyAsync(attn_out, d_out_, bytes, cudaMemcpyDeviceToHost, stream_) !=
+        if (staging_ == Staging::PinnedHost) {
+            if (cudaStreamSynchronize(stream_) != cudaSuccess) return JX_ERR_CUDA;
+            std::memcpy(attn_out, out_, bytes);
+            return JX_OK;
+        }
+        if (cudaMemcpyAsync(attn_out, out_, bytes, cudaMemcpyDeviceToHost, stream_) !=
                 cudaSuccess ||
             cudaStreamSynchronize(stream_) != cudaSuccess)
             return JX_ERR_CUDA;
@@ -283,10 +326,10 @@ class AttentionBlock {
         a.n_seqs = n;
         a.seq_ids = seq;
         a.pos = pos;
-        a.q = d_q_;
-        a.k = d_k_;
-        a.v = d_v_;
-        a.out = d_out_;
+        a.q = q_;
+        a.k = k_;
+        a.v = v_;
+        a.out = out_;
         a.q_stride = hp.q_dim;
         a.kv_stride = hp.kv_dim;
         a.scale = hp.unit_scale ? 1.0f : 1.0f / std::sqrt(static_cast<float>(lw.head_dim));
@@ -299,7 +342,9 @@ class AttentionBlock {
 
     DeviceKVCache& cache_;
     cudaStream_t stream_;
-    float *d_q_ = nullptr, *d_k_ = nullptr, *d_v_ = nullptr, *d_out_ = nullptr;
+    Staging staging_;
+    // q/k/v/out rows: pinned host memory (PinnedHost) or device memory (DeviceCopies)
+    float *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *out_ = nullptr;
     uint32_t rows_ = 0;
     std::vector<int32_t> seq_, pos_;
     int status_ = JX_ERR_INVALID;

@@ -1,7 +1,9 @@
 // Drives jx_engine.hpp the way MoETransformerEngine::forward_token drives its
 // KVCacheSlot and attention block (src/transformer.cpp:2366-2375, 2497-2567,
 // 2792), on host vectors read from a script file; writes every layer's
-// attn_out.  tests/test_gpu_engine.py replays the script through the CPU
+// attn_out.  The optional third argument picks the block's staging
+// (jx::Staging::PinnedHost by default, "copies" for DeviceCopies).
+// tests/test_gpu_engine.py replays the script through the CPU
 // oracle and compares.
 //
 // Script (little-endian): int32 n_layers, n_heads, n_kv_heads, head_dim,
@@ -22,6 +24,7 @@
 // order, float32; then int32 seq_pos, compactions per slot.
 #include <cstdio>
 #include <cstdlib>
+#include <string>
 #include <vector>
 
 #include "jx_engine.hpp"
@@ -29,10 +32,13 @@
 static bool rd(FILE* f, void* p, size_t n) { return fread(p, 1, n, f) == n; }
 
 int main(int argc, char** argv) {
-    if (argc != 3) {
-        fprintf(stderr, "usage: %s script.bin out.bin\n", argv[0]);
+    if (argc != 3 && argc != 4) {
+        fprintf(stderr, "usage: %s script.bin out.bin [pinned|copies]\n", argv[0]);
         return 2;
     }
+    const jx::Staging staging = argc == 4 && std::string(argv[3]) == "copies"
+                                    ? jx::Staging::DeviceCopies
+                                    : jx::Staging::PinnedHost;
     FILE* in = fopen(argv[1], "rb");
     FILE* out = fopen(argv[2], "wb");
     if (!in || !out) return 2;
@@ -58,7 +64,7 @@ int main(int argc, char** argv) {
     std::vector<jx::KVCacheSlot> slots(n_slots);
     for (int s = 0; s < n_slots; ++s)
         if (slots[s].init(s, cache)) return 1;
-    jx::AttentionBlock attn(cache);
+    jx::AttentionBlock attn(cache, nullptr, staging);
     if (attn.status()) return 1;
     std::vector<jx::LayerAttn> layers(L);
     for (int l = 0; l < L; ++l) {

@@ -25,6 +25,7 @@ from tests.helpers import layer_dicts
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 DRIVER = os.path.join(ROOT, "tests", "engine", "drop_in_driver.cpp")
+LATENCY = os.path.join(ROOT, "tests", "engine", "engine_latency.cpp")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 
 # the toy GGUF's shape (models/qwen_run.gguf in the reference): 4 layers,
@@ -33,12 +34,12 @@ L, H, HK, HD, CAP, THETA = 4, 4, 2, 32, 64, 1e6
 TOL = 1e-4
 
 
-def _compile(out_path, syntax_only=False):
+def _compile(out_path, syntax_only=False, src=DRIVER):
     cxx = shutil.which("g++")
     if cxx is None:
         pytest.skip("g++ not available")
     cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-I", os.path.join(ROOT, "include"),
-           "-I", os.path.join(CUDA_HOME, "include"), DRIVER]
+           "-I", os.path.join(CUDA_HOME, "include"), src]
     if syntax_only:
         cmd += ["-fsyntax-only"]
     else:
@@ -53,6 +54,25 @@ def test_engine_header_and_driver_compile():
     if not os.path.exists(os.path.join(CUDA_HOME, "include", "cuda_runtime.h")):
         pytest.skip("CUDA headers not available")
     _compile(None, syntax_only=True)
+    _compile(None, syntax_only=True, src=LATENCY)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("staging", ["pinned", "copies"])
+def test_engine_latency_driver_runs(staging):
+    # the per-token latency driver bench.py --engine uses: a few tokens of a
+    # small shape, both staging modes; it checks the device error word itself
+    import json
+    import jxai_b200 as jx
+    jx.load_library()
+    with tempfile.TemporaryDirectory() as td:
+        exe = os.path.join(td, "latency")
+        _compile(exe, src=LATENCY)
+        r = subprocess.run([exe, "2", "300", "3", "8", "2", "64", "1", "10000", "4", "2", staging],
+                           capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    d = json.loads(r.stdout.strip().splitlines()[-1])
+    assert d["tokens"] == 4 and d["staging"] == staging and d["ms_per_token"] > 0
 
 
 def _tok(rng, n=None):
@@ -87,7 +107,7 @@ def _write_script(path, n_slots, ops):
                 v[l].tofile(f)
 
 
-def _run_driver(n_slots, ops):
+def _run_driver(n_slots, ops, staging="pinned"):
     import jxai_b200 as jx
     jx.load_library()  # builds the library if needed
     with tempfile.TemporaryDirectory() as td:
@@ -95,7 +115,8 @@ def _run_driver(n_slots, ops):
         _compile(exe)
         script, outp = os.path.join(td, "script.bin"), os.path.join(td, "out.bin")
         _write_script(script, n_slots, ops)
-        r = subprocess.run([exe, script, outp], capture_output=True, text=True, timeout=300)
+        r = subprocess.run([exe, script, outp, staging], capture_output=True, text=True,
+                           timeout=300)
         assert r.returncode == 0, r.stderr
         got = np.fromfile(outp, dtype=np.uint8)
     tail = got[len(got) - 8 * n_slots:].view(np.int32).reshape(n_slots, 2)
@@ -143,20 +164,24 @@ def _replay(n_slots, ops):
 
 
 @pytest.mark.gpu
-def test_engine_drop_in_matches_oracle_over_a_token_stream():
+@pytest.mark.parametrize("staging", ["pinned", "copies"])
+def test_engine_drop_in_matches_oracle_over_a_token_stream(staging):
     # 50 tokens, prefix reuse back to 30, 60 more tokens (crosses the 64-row
-    # capacity: one compaction); slot 1 of 2, so the slot id reaches the library
+    # capacity: one compaction); slot 1 of 2, so the slot id reaches the library.
+    # Both staging modes of the block: pinned host rows read/written by the
+    # library, and device copies through cudaMemcpyAsync.
     rng = np.random.default_rng(2024)
     ops = [("tok", 1, _tok(rng)) for _ in range(50)] + [("lcp", 1, 30)]
     ops += [("tok", 1, _tok(rng)) for _ in range(60)]
-    got, tail = _run_driver(2, ops)
+    got, tail = _run_driver(2, ops, staging)
     ref, ref_tail = _replay(2, ops)
     assert np.abs(got - ref).max() <= TOL
     assert (tail == ref_tail).all() and tail[1, 1] == 1
 
 
 @pytest.mark.gpu
-def test_engine_batched_slots_and_prompts_match_oracle():
+@pytest.mark.parametrize("staging", ["pinned", "copies"])
+def test_engine_batched_slots_and_prompts_match_oracle(staging):
     # four slots: prompts of different lengths (forward_prompt), then batched
     # decode over changing subsets of slots (forward_batch), a rollback, and
     # enough batched tokens that two slots compact on overflow
@@ -170,7 +195,7 @@ def test_engine_batched_slots_and_prompts_match_oracle():
     ops.append(("prompt", 0, _tok(rng, 6)))
     for _ in range(8):
         ops.append(("batch", [3, 2, 1, 0], _tok(rng, 4)))
-    got, tail = _run_driver(4, ops)
+    got, tail = _run_driver(4, ops, staging)
     ref, ref_tail = _replay(4, ops)
     assert got.shape == ref.shape
     assert np.abs(got - ref).max() <= TOL
