@@ -21,6 +21,7 @@
 #include <mutex>
 #include <string>
 #include <tuple>
+#include <type_traits>
 #include <vector>
 
 #include "jx_attn.h"
@@ -214,26 +215,46 @@ void default_shape(int hd, int gp, int kp, int dtype, int* stages, int* cps) {
     *cps = 1;
 }
 
-// (cos, sin) of every rotated pair at `pos`, computed with the same float
-// expressions as apply_rope (src/transformer.cpp:82-92, 112-116).
-void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
-              bool neox, const float* rope_freqs, float2* out, int width) {
+// Inverse frequency of every rotated pair (half = min(head_dim, rope_dim) / 2
+// entries), computed with the same float expressions as apply_rope
+// (src/transformer.cpp:82-92, 112-116).  It does not depend on the position,
+// so a step computes it once per RoPE configuration.
+void rope_inv_freqs(uint32_t head_dim, uint32_t rope_dim, float base, bool neox,
+                    const float* rope_freqs, float* freq) {
     const uint32_t rdim = std::min(head_dim, rope_dim);
-    const float pos_scaled = static_cast<float>(pos) / std::max(1e-4f, yarn_scale);
     const uint32_t half = rdim / 2;
-    for (int j = 0; j < width; ++j) out[j] = make_float2(0.0f, 0.0f);
     for (uint32_t j = 0; j < half; ++j) {
-        float freq;
+        float f;
         if (neox) {
-            freq = 1.0f / std::pow(base, (2.0f * static_cast<float>(j)) / static_cast<float>(rdim));
-            if (rope_freqs) freq /= rope_freqs[j];
+            f = 1.0f / std::pow(base, (2.0f * static_cast<float>(j)) / static_cast<float>(rdim));
+            if (rope_freqs) f /= rope_freqs[j];
         } else {
             const uint32_t d = 2 * j;
-            freq = 1.0f / std::pow(base, static_cast<float>(d) / static_cast<float>(rdim));
+            f = 1.0f / std::pow(base, static_cast<float>(d) / static_cast<float>(rdim));
         }
-        const float angle = pos_scaled * freq;
+        freq[j] = f;
+    }
+}
+
+// (cos, sin) of the `half` rotated pairs at `pos` from their inverse
+// frequencies; writes `width` entries (zeros past the rotated pairs).
+void rope_row_freqs(const float* freq, uint32_t half, uint32_t pos, float yarn_scale, float2* out,
+                    int width) {
+    const float pos_scaled = static_cast<float>(pos) / std::max(1e-4f, yarn_scale);
+    for (int j = 0; j < width; ++j) out[j] = make_float2(0.0f, 0.0f);
+    for (uint32_t j = 0; j < half; ++j) {
+        const float angle = pos_scaled * freq[j];
         out[j] = make_float2(std::cos(angle), std::sin(angle));
     }
+}
+
+// (cos, sin) of every rotated pair at `pos`, as apply_rope computes them.
+void rope_row(uint32_t head_dim, uint32_t rope_dim, uint32_t pos, float base, float yarn_scale,
+              bool neox, const float* rope_freqs, float2* out, int width) {
+    float freq[128];  // head_dim <= 256
+    const uint32_t half = std::min(std::min(head_dim, rope_dim) / 2, 128u);
+    rope_inv_freqs(std::min(head_dim, 256u), rope_dim, base, neox, rope_freqs, freq);
+    rope_row_freqs(freq, half, pos, yarn_scale, out, width);
 }
 
 }  // namespace jx
@@ -530,7 +551,14 @@ std::vector<long long> balanced_split(const std::vector<long long>& seg_off, lon
         b[static_cast<size_t>(P)] = total;
         return b;
     }
-    auto layout = [&](double budget_rows, bool write) -> long long {
+    // One layout pass for a per-CTA budget: CTA boundaries (write) and how
+    // far the P slices reach.  With kRuns, a run of fresh CTAs that each end
+    // inside the current segment takes `step` rows apiece and is laid out at
+    // once, so a pass costs O(segments) rather than O(P) where segments are
+    // long (a pass runs a dozen times per bisection, on every call whose plan
+    // changed); both forms give the same boundaries.
+    auto layout = [&](double budget_rows, bool write, auto runs) -> long long {
+        const long long step = static_cast<long long>(budget_rows);  // rows of a fresh CTA
         long long x = 0;
         size_t j = 0;  // seg_off[j] <= x < seg_off[j+1]
         for (long long c = 0; c < P; ++c) {
@@ -541,6 +569,26 @@ std::vector<long long> balanced_split(const std::vector<long long>& seg_off, lon
                 const long long seg_end = seg_off[j + 1];
                 const long long avail = seg_end - x;
                 if (static_cast<double>(avail) >= budget) {
+                    if constexpr (decltype(runs)::value) {
+                        if (budget == budget_rows && step > 0 &&
+                            static_cast<double>(avail) >= 4.0 * budget_rows) {
+                            // CTA i of the run needs avail - i*step >= budget_rows
+                            long long k = static_cast<long long>(
+                                              (static_cast<double>(avail) - budget_rows) /
+                                              static_cast<double>(step)) + 1;
+                            while (k > 1 &&
+                                   static_cast<double>(avail - (k - 1) * step) < budget_rows)
+                                --k;
+                            while (static_cast<double>(avail - k * step) >= budget_rows) ++k;
+                            k = std::min(k, P - c);
+                            if (write)
+                                for (long long i = 1; i < k; ++i)
+                                    b[static_cast<size_t>(c + i)] = x + i * step;
+                            x += k * step;
+                            c += k - 1;
+                            break;
+                        }
+                    }
                     x += static_cast<long long>(budget);
                     break;
                 }
@@ -552,13 +600,19 @@ std::vector<long long> balanced_split(const std::vector<long long>& seg_off, lon
         if (write) b[static_cast<size_t>(P)] = total;
         return x;
     };
+    // runs pay off when a CTA's share is well under a segment
+    const bool long_segments = P >= 4 * static_cast<long long>(m);
+    auto pass = [&](double budget_rows, bool write) -> long long {
+        return long_segments ? layout(budget_rows, write, std::true_type{})
+                             : layout(budget_rows, write, std::false_type{});
+    };
     double lo = static_cast<double>(total) / static_cast<double>(P);
     double hi = lo + penalty * static_cast<double>(m) + 1.0;
     for (int it = 0; it < 60 && hi - lo > 0.5; ++it) {
         const double mid = 0.5 * (lo + hi);
-        if (layout(mid, false) >= total) hi = mid; else lo = mid;
+        if (pass(mid, false) >= total) hi = mid; else lo = mid;
     }
-    layout(hi, true);
+    pass(hi, true);
     return b;
 }
 
@@ -721,6 +775,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         std::map<std::tuple<uint32_t, uint32_t, uint32_t, uint32_t, uint64_t, uint32_t>, int>
             rope_ids;
         std::vector<float2> rope;
+        // inverse frequencies per RoPE configuration (rotated dims, base, factors)
+        std::map<std::tuple<uint32_t, uint32_t, uint64_t>, std::vector<float>> inv_freqs;
         const int width = hd / 2;
         int n_rope_rows = 0;
         // step rows grouped into blocks (first row, tokens): single rows, or
@@ -788,10 +844,18 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                     rope_ids.emplace(key, rid);
                     n_rope_rows += static_cast<int>(nb);
                     rope.resize(static_cast<size_t>(n_rope_rows) * width);
+                    // the configuration's inverse frequencies, once per call
+                    const auto fkey = std::make_tuple(rdim, base_bits, fh);
+                    auto itf = inv_freqs.find(fkey);
+                    if (itf == inv_freqs.end()) {
+                        std::vector<float> f(rdim / 2);
+                        rope_inv_freqs(L.head_dim, L.rope_dim, L.rope_freq_base, neox, rf,
+                                       f.data());
+                        itf = inv_freqs.emplace(fkey, std::move(f)).first;
+                    }
                     for (uint32_t j = 0; j < nb; ++j)
-                        rope_row(L.head_dim, L.rope_dim, pos + j, L.rope_freq_base, a->yarn_scale,
-                                 neox, rf, rope.data() + static_cast<size_t>(rid + j) * width,
-                                 width);
+                        rope_row_freqs(itf->second.data(), rdim / 2, pos + j, a->yarn_scale,
+                                       rope.data() + static_cast<size_t>(rid + j) * width, width);
                 } else {
                     rid = itk->second;
                 }
