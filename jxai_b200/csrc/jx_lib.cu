@@ -27,6 +27,7 @@
 #include "jx_attn.h"
 #include "jx_device.cuh"
 #include "jx_internal.h"
+#include "jx_plan.h"
 
 namespace jx {
 bool decode_dispatch_dt0(int, int, int, int, int, const DecodeLaunch*, int*, cudaError_t*);
@@ -513,107 +514,6 @@ double split_rows_per_us(const jx_kv* kv, size_t bytes_per_row, long long P) {
     (void)kv;
     if (bytes_per_row == 0 || P <= 0) return 0.0;
     return 6.5e6 / static_cast<double>(P) / static_cast<double>(bytes_per_row);
-}
-
-// Slice boundaries b[0..P] over the flattened rows (segment j starts at
-// seg_off[j], seg_off.back() == total) so that every CTA's rows plus
-// `penalty` rows per extra piece (each segment boundary inside its slice)
-// come out equal.
-//  * Few segments per CTA: the smallest per-CTA budget that covers every row,
-//    by bisection (each step a walk over the CTAs and segments).
-//  * Many (a prefill's thousands of short segments): one pass -- with
-//    F(x) = x + penalty * (segment starts <= x), CTA c takes
-//    [F^-1(c*C/P), F^-1((c+1)*C/P)), C = F(total).  Here a CTA's share is
-//    much larger than one penalty, so no CTA falls inside a single step of F
-//    (which would leave it empty).
-std::vector<long long> balanced_split(const std::vector<long long>& seg_off, long long total,
-                                      long long P, double penalty) {
-    std::vector<long long> b(static_cast<size_t>(P) + 1, total);
-    const size_t m = seg_off.size() - 1;  // segments
-    b[0] = 0;
-    if (m == 0 || P <= 1) return b;
-    if (m > static_cast<size_t>(64 * P)) {
-        std::vector<double> F(m);  // F just after segment j's start
-        for (size_t j = 0; j < m; ++j)
-            F[j] = static_cast<double>(seg_off[j]) + penalty * static_cast<double>(j + 1);
-        const double C = static_cast<double>(total) + penalty * static_cast<double>(m);
-        for (long long c = 1; c < P; ++c) {
-            const double target = C * static_cast<double>(c) / static_cast<double>(P);
-            const size_t j = static_cast<size_t>(
-                std::upper_bound(F.begin(), F.end(), target) - F.begin());
-            long long x = 0;
-            if (j > 0) {
-                const size_t sj = j - 1;
-                x = std::min(seg_off[sj] + static_cast<long long>(target - F[sj]), seg_off[sj + 1]);
-            }
-            b[static_cast<size_t>(c)] = std::max(x, b[static_cast<size_t>(c - 1)]);
-        }
-        b[static_cast<size_t>(P)] = total;
-        return b;
-    }
-    // One layout pass for a per-CTA budget: CTA boundaries (write) and how
-    // far the P slices reach.  With kRuns, a run of fresh CTAs that each end
-    // inside the current segment takes `step` rows apiece and is laid out at
-    // once, so a pass costs O(segments) rather than O(P) where segments are
-    // long (a pass runs a dozen times per bisection, on every call whose plan
-    // changed); both forms give the same boundaries.
-    auto layout = [&](double budget_rows, bool write, auto runs) -> long long {
-        const long long step = static_cast<long long>(budget_rows);  // rows of a fresh CTA
-        long long x = 0;
-        size_t j = 0;  // seg_off[j] <= x < seg_off[j+1]
-        for (long long c = 0; c < P; ++c) {
-            if (write) b[static_cast<size_t>(c)] = x;
-            double budget = budget_rows;
-            while (x < total) {
-                while (j + 1 < seg_off.size() && seg_off[j + 1] <= x) ++j;
-                const long long seg_end = seg_off[j + 1];
-                const long long avail = seg_end - x;
-                if (static_cast<double>(avail) >= budget) {
-                    if constexpr (decltype(runs)::value) {
-                        if (budget == budget_rows && step > 0 &&
-                            static_cast<double>(avail) >= 4.0 * budget_rows) {
-                            // CTA i of the run needs avail - i*step >= budget_rows
-                            long long k = static_cast<long long>(
-                                              (static_cast<double>(avail) - budget_rows) /
-                                              static_cast<double>(step)) + 1;
-                            while (k > 1 &&
-                                   static_cast<double>(avail - (k - 1) * step) < budget_rows)
-                                --k;
-                            while (static_cast<double>(avail - k * step) >= budget_rows) ++k;
-                            k = std::min(k, P - c);
-                            if (write)
-                                for (long long i = 1; i < k; ++i)
-                                    b[static_cast<size_t>(c + i)] = x + i * step;
-                            x += k * step;
-                            c += k - 1;
-                            break;
-                        }
-                    }
-                    x += static_cast<long long>(budget);
-                    break;
-                }
-                x = seg_end;
-                budget -= static_cast<double>(avail) + penalty;
-                if (budget <= 0.0) break;
-            }
-        }
-        if (write) b[static_cast<size_t>(P)] = total;
-        return x;
-    };
-    // runs pay off when a CTA's share is well under a segment
-    const bool long_segments = P >= 4 * static_cast<long long>(m);
-    auto pass = [&](double budget_rows, bool write) -> long long {
-        return long_segments ? layout(budget_rows, write, std::true_type{})
-                             : layout(budget_rows, write, std::false_type{});
-    };
-    double lo = static_cast<double>(total) / static_cast<double>(P);
-    double hi = lo + penalty * static_cast<double>(m) + 1.0;
-    for (int it = 0; it < 60 && hi - lo > 0.5; ++it) {
-        const double mid = 0.5 * (lo + hi);
-        if (pass(mid, false) >= total) hi = mid; else lo = mid;
-    }
-    pass(hi, true);
-    return b;
 }
 
 // q/k/v/out (and partials) may live in this device's memory or in pinned

@@ -44,3 +44,23 @@ def test_position_shards_cover_the_sequence(n):
     assert sh[0][0] == 0 and sh[-1][1] == 131072
     assert all(a[1] == b[0] for a, b in zip(sh, sh[1:]))
     assert max(e - b for b, e in sh) - min(e - b for b, e in sh) <= 1
+
+
+def test_slice_planner_boundaries_and_layout_forms(tmp_path):
+    # jx::balanced_split (jxai_b200/csrc/jx_plan.h) sizes the persistent CTAs'
+    # slices of a step; built with g++ alone and checked on seeded random
+    # layouts (tests/host/plan_check.cpp)
+    import os
+    import shutil
+    import subprocess
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("g++ not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "plan_check")
+    subprocess.run([cxx, "-std=c++17", "-O2", "-Wall", "-I", os.path.join(root, "jxai_b200", "csrc"),
+                    os.path.join(root, "tests", "host", "plan_check.cpp"), "-o", exe],
+                   check=True, capture_output=True, text=True)
+    r = subprocess.run([exe, "20000"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.startswith("ok ")
