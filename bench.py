@@ -61,6 +61,9 @@ def parse_args():
                         "one synchronous block call per layer on host vectors, as forward_token\n"
                         "makes it; single-sequence full-attention configs (c1, c2, c4)")
     p.add_argument("--tokens", type=int, default=200, help="timed tokens of --engine")
+    p.add_argument("--prefill", type=int, default=0, metavar="N",
+                   help="prompt throughput: one prompt of N tokens per jx_attn_prefill call\n"
+                        "(full-attention configs), the reference's token-serial loop beside it")
     return p.parse_args()
 
 
@@ -646,6 +649,109 @@ def run_engine(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args, rank, world):
+    """Prompt throughput: one prompt of --prefill tokens per jx_attn_prefill call.
+
+    jxai feeds a prompt token by token through forward_token
+    (src/transformer.cpp:3092-3095): each token appends its row and attends
+    over every earlier one.  jx_attn_prefill takes the whole prompt in one
+    call (every row appended, then each token attends causally).  The
+    reference's own token-serial CPU loop is timed beside it on the last
+    tokens of the same prompt (the cache rows before them filled with seeded
+    values) and projected to the whole prompt by the rows it reads.
+    """
+    if rank != 0:
+        return
+    import torch
+    import jxai_b200 as jx
+    w = W.make(args.config, args.dtype)
+    if w.window:
+        raise SystemExit("--prefill runs the full-attention configs (c1..c4)")
+    N = args.prefill
+    w.lengths = [N]  # the prompt: positions 0 .. N-1
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cache = jx.KVCache(1, w.n_layers, N, w.kv_dim, w.dtype, 0)
+    q = torch.empty(N, w.n_layers, w.q_dim, device=dev)
+    k = torch.empty(N, w.n_layers, w.kv_dim, device=dev)
+    v = torch.empty_like(k)
+    jx.fill_normal(q, W.SEED, 3)
+    jx.fill_normal(k, W.SEED, 4)
+    jx.fill_normal(v, W.SEED, 5)
+    out = torch.empty_like(q)
+    pos = list(range(N))
+
+    def call():
+        jx.attn_prefill(cache, w.layers, q, k, v, out, pos, w.n_heads, w.n_kv_heads,
+                        scale=w.scale, neox=w.neox)
+
+    for _ in range(max(3, args.warmup)):
+        call()
+    torch.cuda.synchronize()
+    K = max(1, min(args.steps, 50))
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(K):
+        call()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / K
+    if cache.check_device_error():
+        raise RuntimeError("device error during the prefill timing")
+    launches = cache.last_launch_count() + 1  # the append launch is not counted there
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle.oracle import BF16, F16T, F32
+        orc, kind = _cpu_oracle()
+        dt = {"f32": F32, "bf16": BF16, "f16": F16T}[w.dtype]
+        rng = np.random.default_rng(W.SEED)
+        shape = (1, w.n_layers, N, w.kv_dim)
+        if dt == F32:
+            kc = rng.standard_normal(shape, dtype=np.float32)
+            vc = rng.standard_normal(shape, dtype=np.float32)
+        else:
+            kc = (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+            vc = (rng.standard_normal(shape, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        qh = rng.standard_normal((N, w.n_layers, w.q_dim), dtype=np.float32)
+        kh = rng.standard_normal((N, w.n_layers, w.kv_dim), dtype=np.float32)
+        vh = rng.standard_normal((N, w.n_layers, w.kv_dim), dtype=np.float32)
+        layers = [dict(rope_dim=L.rope_dim, rope_base=L.rope_base, is_swa=0, shares_kv=0,
+                       kv_source_layer=i) for i, L in enumerate(w.layers)]
+
+        def token(t):
+            orc.step(kc, vc, dt, [t], layers, qh[t][None], kh[t][None], vh[t][None], w.n_heads,
+                     w.n_kv_heads, w.head_dim, w.scale, 0.0, 0, 1.0, w.neox)
+
+        token(N - 1)  # warm-up (thread pool, pages)
+        t0 = time.perf_counter()
+        token(N - 1)
+        one = time.perf_counter() - t0
+        n_s = int(min(N, max(1, args.cpu_sample_s / max(one, 1e-6))))
+        t0 = time.perf_counter()
+        for t in range(N - n_s, N):
+            token(t)
+        el = time.perf_counter() - t0
+        rows_sample = sum(t + 1 for t in range(N - n_s, N))
+        rows_full = N * (N + 1) // 2
+        cpu_ms = el * 1e3 * rows_full / rows_sample
+        cpu = {"value": round(N / (cpu_ms * 1e-3), 2), "unit": "tokens/s",
+               "ms_per_prompt": round(cpu_ms, 2), "cores": orc.max_threads(), "kind": kind,
+               "sample": f"token-serial loop over the last {n_s} of {N} positions "
+                         f"({el:.2f} s), projected to the whole prompt by rows read"}
+    line = {
+        "metric": "prefill tokens/s", "value": round(N / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": 1, "steps": K, "warmup": max(3, args.warmup), "ms_per_prompt": round(ms, 4),
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-side)",
+        "config": dict(w.describe(), prompt_tokens=N,
+                       path="jx_attn_prefill: the whole prompt per call (append launch, then "
+                            "causal attention; 8/G consecutive tokens share a pass over their rows)"),
+        "gpu_launches": launches * K, "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -656,6 +762,9 @@ def main():
         return
     if args.engine:
         run_engine(args, rank, world)
+        return
+    if args.prefill > 0:
+        run_prefill(args, rank, world)
         return
     import torch
     import torch.distributed as dist
