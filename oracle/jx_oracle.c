@@ -13,8 +13,8 @@
  * fused multiply-add that the reference's own build (-O3 -mavx2 -mfma, GNU
  * C++20, gcc 13) forms is written as fmaf().  The forms were established by
  * comparing against the reference's compiled apply_rope over 2.4M rotated
- * pairs, and tests/test_oracle_pin.py re-checks them bit for bit against the
- * reference build in oracle/_ref/ whenever that build exists.
+ * pairs, and tests/test_oracle_golden.py re-checks them bit for bit against
+ * fixtures the reference build in oracle/_ref/ produced (tests/golden/).
  */
 #include <math.h>
 #include <stdint.h>

@@ -1,4 +1,5 @@
-"""Host-side logic: workload definitions, byte accounting, partitioning."""
+"""Host-side logic: workload definitions, byte accounting, partitioning, the
+slice planner, and sanitizer (ASan + UBSan) runs of the planner and the CPU oracle."""
 import numpy as np
 import pytest
 
@@ -63,4 +64,47 @@ def test_slice_planner_boundaries_and_layout_forms(tmp_path):
                    check=True, capture_output=True, text=True)
     r = subprocess.run([exe, "20000"], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.startswith("ok ")
+
+
+def _san_flags():
+    return ["-g", "-O1", "-fsanitize=address,undefined,float-cast-overflow",
+            "-fno-sanitize-recover=all"]
+
+
+def test_oracle_under_sanitizers(tmp_path):
+    # the CPU oracle built with AddressSanitizer + UndefinedBehaviorSanitizer
+    # (OpenMP on) and run over every exported function (tests/host/oracle_san.c)
+    import os
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("gcc not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "oracle_san")
+    subprocess.run([cc, "-std=c11", "-ffp-contract=off", "-fopenmp", *_san_flags(),
+                    os.path.join(root, "oracle", "jx_oracle.c"),
+                    os.path.join(root, "tests", "host", "oracle_san.c"), "-o", exe, "-lm"],
+                   check=True, capture_output=True, text=True)
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stdout + r.stderr[-3000:]
+    assert r.stdout.startswith("ok ")
+
+
+def test_slice_planner_under_sanitizers(tmp_path):
+    import os
+    import shutil
+    import subprocess
+    cxx = shutil.which("g++")
+    if cxx is None:
+        pytest.skip("g++ not available")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = str(tmp_path / "plan_check_san")
+    subprocess.run([cxx, "-std=c++17", *_san_flags(), "-I", os.path.join(root, "jxai_b200", "csrc"),
+                    os.path.join(root, "tests", "host", "plan_check.cpp"), "-o", exe],
+                   check=True, capture_output=True, text=True)
+    r = subprocess.run([exe, "3000"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr[-3000:]
     assert r.stdout.startswith("ok ")
