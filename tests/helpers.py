@@ -30,3 +30,28 @@ def oracle_step(kc, vc, dtype, pos, layers, q, k, v, n_heads, n_kv, head_dim, sc
     """Runs the CPU oracle in place on host caches; returns out."""
     return Oracle(kind).step(kc, vc, dtype, pos, layer_dicts(layers), q, k, v, n_heads, n_kv,
                              head_dim, scale, softcap, window, yarn, neox, rope_freqs)
+
+
+_M64 = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+
+def _splitmix64(x):
+    x = x + np.uint64(0x9E3779B97F4A7C15)
+    x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+    x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return x ^ (x >> np.uint64(31))
+
+
+def normal_at(seed: int, stream_id: int, idx) -> np.ndarray:
+    """Host restatement of the library's seeded fill (jx_lib.cu normal_at):
+    splitmix64 of (seed, stream, index), then Box-Muller.  The device uses
+    logf / cospif in float32, this float64 numpy, so values agree to a few
+    float32 ulps -- enough to rebuild the unrounded values behind a bf16 cache
+    for the 2e-2 bar, not for bit-level checks."""
+    with np.errstate(over="ignore"):
+        idx = np.asarray(idx, dtype=np.uint64)
+        inner = _splitmix64((np.uint64(stream_id) << np.uint64(56)) ^ idx)
+        h = _splitmix64(np.uint64(seed) ^ inner)
+    u1 = ((h >> np.uint64(40)).astype(np.float64) + 1.0) / 16777216.0
+    u2 = (h & np.uint64(0xFFFFFF)).astype(np.float64) / 16777216.0
+    return (np.sqrt(-2.0 * np.log(u1)) * np.cos(2.0 * np.pi * u2)).astype(np.float32)

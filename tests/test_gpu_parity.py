@@ -290,3 +290,92 @@ def test_repeated_and_alternating_calls():
         assert np.abs(out.cpu().numpy() - ref).max() <= TOL, seq
     assert cache.check_device_error() == 0
     cache.close()
+
+
+def _mixed_case(layers, cache_layers, n_heads, n_kv, lengths, dtype, seed, hd_max, options=None):
+    """One jx_attn_step over `layers` (a mix of head dims and shares-KV layers)
+    against the oracle run layer by layer in call order, as forward_token runs
+    them (src/transformer.cpp:2442, 2512): a sharing layer reads its source
+    layer's cache after that layer appended this step's row."""
+    import jxai_b200 as jx
+    torch = _torch()
+    from oracle.oracle import Oracle
+    from tests.helpers import layer_dicts
+    rng = np.random.default_rng(seed)
+    n_seqs, L = len(lengths), len(layers)
+    cap = max(lengths) + 2
+    rs = n_kv * hd_max
+    qs, ks = n_heads * hd_max, n_kv * hd_max
+    kc = random_cache(rng, (n_seqs, cache_layers, cap, rs), dtype)
+    vc = random_cache(rng, (n_seqs, cache_layers, cap, rs), dtype)
+    q = rng.standard_normal((n_seqs, L, qs)).astype(np.float32)
+    k = rng.standard_normal((n_seqs, L, ks)).astype(np.float32)
+    v = rng.standard_normal((n_seqs, L, ks)).astype(np.float32)
+    pos = [T - 1 for T in lengths]
+    cache = jx.KVCache(n_seqs, cache_layers, cap, rs, dtype)
+    for key, val in (options or {}).items():
+        cache.set_option(key, val)
+    for s in range(n_seqs):
+        for l in range(cache_layers):
+            cache.write_rows(s, l, 0, 0, kc[s, l])
+            cache.write_rows(s, l, 1, 0, vc[s, l])
+    qd, kd, vd = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    out = torch.full_like(qd, float("nan"))
+    # scale 1/sqrt(64) for every layer (the step takes one scale)
+    jx.attn_step(cache, layers, qd, kd, vd, out, pos, n_heads, n_kv, scale=0.125, neox=True)
+    torch.cuda.synchronize()
+    assert cache.check_device_error() == 0
+    launches = cache.last_launch_count()
+    got = out.cpu().numpy()
+    ko, vo = kc.copy(), vc.copy()
+    orc = Oracle("port")
+    ref = np.zeros_like(got)
+    for l, Ld in enumerate(layers):
+        ref[:, l:l + 1] = orc.step(ko, vo, dtype, pos, layer_dicts([Ld]), q[:, l:l + 1],
+                                   k[:, l:l + 1], v[:, l:l + 1], n_heads, n_kv, Ld.head_dim,
+                                   0.125, 0.0, 0, 1.0, True)
+    for s in range(n_seqs):
+        for l in range(cache_layers):
+            gk = cache.read_rows(s, l, 0, 0, cap)
+            gv = cache.read_rows(s, l, 1, 0, cap)
+            assert np.array_equal(gk.view(np.uint8), ko[s, l].view(np.uint8)), (s, l, "K")
+            assert np.array_equal(gv.view(np.uint8), vo[s, l].view(np.uint8)), (s, l, "V")
+    for l, Ld in enumerate(layers):
+        w = n_heads * Ld.head_dim
+        err = np.abs(got[:, l, :w] - ref[:, l, :w]).max()
+        assert np.isfinite(got[:, l, :w]).all(), l
+        assert err <= TOL, f"layer {l}: max-abs {err}"
+    cache.close()
+    return launches
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16, F16T])
+@pytest.mark.parametrize("pdl", [0, 1])
+def test_shared_kv_layers(dtype, pdl):
+    # Gemma-3n/4 style shared-KV layers (src/transformer.cpp:2127-2137): a
+    # sharing layer appends nothing and reads its source layer's cache.  Layers
+    # 2 and 4 read cache layers 0 and 1, appended by layers 0 and 1 of the same
+    # call (a second launch that must see those appends); layer 3 reads cache
+    # layer 5, which no layer of the call appends (first launch).  Cache layers
+    # 2, 3 and 4 stay untouched.
+    import jxai_b200 as jx
+    hd = 64
+    layers = [jx.Layer(hd, hd, 1e6, 0), jx.Layer(hd, hd, 1e4, 1),
+              jx.Layer(hd, hd, 1e6, 0, shares_kv=True),
+              jx.Layer(hd, hd, 1e6, 5, shares_kv=True),
+              jx.Layer(hd, hd, 1e4, 1, shares_kv=True), jx.Layer(hd, hd, 1e6, 6)]
+    n = _mixed_case(layers, 7, 8, 2, [300, 41, 7], dtype, seed=31 + dtype, hd_max=hd,
+                    options={"pdl": pdl, "grid": 9})
+    assert n == 2
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_mixed_head_dims_in_one_call(dtype):
+    # layers of different head_dim (as Gemma-3n's per-layer head sizes): one
+    # launch per head_dim in one call, all sharing the q / kv strides
+    import jxai_b200 as jx
+    layers = [jx.Layer(64, 64, 1e6, 0), jx.Layer(128, 128, 1e4, 1), jx.Layer(64, 64, 1e6, 2),
+              jx.Layer(128, 128, 1e6, 3, shares_kv=True), jx.Layer(128, 128, 1e6, 1,
+                                                                    shares_kv=True)]
+    n = _mixed_case(layers, 4, 8, 2, [257, 66], dtype, seed=41 + dtype, hd_max=128)
+    assert n == 3  # hd 64, hd 128 (incl. the sharer of layer 3), then the sharer of layer 1
