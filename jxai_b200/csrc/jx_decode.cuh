@@ -96,7 +96,7 @@ struct SmemLayout {
     static constexpr int ml_bytes = kConsumerWarps * GS * 2 * 4;
     static constexpr int lohi_bytes = 2 * GS * 4;       // per-column row limits (prefill blocks)
     static constexpr int misc_bytes = 16 + 2 * 48 + 48;  // flags, two split records, new-row record
-    static constexpr int n_extra_bars = 4;              // q full[2], q empty[2]
+    static constexpr int n_extra_bars = 5;  // q full[2], q empty[2], test (never arrived at)
     static __host__ __device__ constexpr int stages_bytes(int ns) { return ns * 2 * G::TILEB; }
     static __host__ __device__ constexpr int bars_offset(int ns) {
         return stages_bytes(ns) + q_bytes + qraw_bytes + rope_bytes + p_bytes + o_bytes +
@@ -677,10 +677,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     const uint32_t bars = base_u32 + L::bars_offset(NS);
     const uint32_t qfull = bars + 8 * (2 * NS);
     const uint32_t qempty = qfull + 16;
+    const uint32_t test_bar = qempty + 16;  // nothing ever arrives here
     volatile int* abort_flag = misc + 1;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // bound of every pipeline wait (0 in the arguments: the default)
+    const long long wlim = a.wait_limit > 0 ? a.wait_limit : kWaitLimitCycles;
     // The next step may be scheduled onto SMs as this grid frees them; it
     // waits (pdl_wait) for this grid's completion before touching any data.
     pdl_launch_dependents();
@@ -701,6 +704,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             mbar_init(qfull + 8 * s, 1);
             mbar_init(qempty + 8 * s, 1);
         }
+        mbar_init(test_bar, 1);
         misc[0] = 0;
         misc[1] = 0;
         fence_barrier_init();
@@ -751,7 +755,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 const int qs = piece & 1;
                 if (piece >= 2)
                     mbar_wait_bounded(qempty + 8 * qs, ((piece >> 1) & 1) ^ 1u, abort_flag, a.err,
-                                      a.dbg, 4, piece);
+                                      a.dbg, 4, piece, true, wlim);
                 if (lane == 0 && *abort_flag == 0 &&
                     JX_CHECKED(a, pr.io >= 0 && pr.io < a.n_io && pr.rope_row >= 0 &&
                                       pr.rope_row < a.n_rope_rows &&
@@ -792,7 +796,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                 // wait until the previous use of this stage (tile - NS) has been released
                 if (tile >= NS)
                     mbar_wait_bounded(bars + 8 * (NS + cur_stage), cur_phase ^ 1u, abort_flag,
-                                      a.err, a.dbg, 1, tile);
+                                      a.err, a.dbg, 1, tile, true, wlim);
                 const bool issue = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
                 if (!issue) continue;
                 n_issued = tile + 1;
@@ -837,6 +841,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
     // ---------------------------------------------------------------- consumers
     const int ctid = threadIdx.x;
     pdl_wait();  // outputs, partials and counters were last written by an earlier step
+    if (a.test_wait_cta > 0 && blockIdx.x == a.test_wait_cta - 1 && warp == 0) {
+        // Test hook for the error path: one bounded wait on a barrier nothing
+        // arrives at.  It runs out after wlim cycles, raises the CTA's
+        // abort flag and the device error word; every later wait of the CTA
+        // then returns at once and the CTA finishes its control flow.
+        mbar_wait_bounded(test_bar, 0u, abort_flag, a.err, a.dbg, 7, 0, true, wlim);
+    }
 
     // Partial mode: pairs with no local rows still owe an (o=0, m=-inf, l=0) partial.
     if (a.part_out) {
@@ -930,7 +941,7 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         if (a.q_bulk) {
             const int qs = qs_piece;
             mbar_wait_bounded(qfull + 8 * qs, (cpiece >> 1) & 1, abort_flag, a.err, a.dbg, 5,
-                              cpiece);
+                              cpiece, true, wlim);
             const float* qr = qraw_s + qs * GS * HD;
             const float2* cs = rope_s + qs * (HD / 2);
             for (int idx = ctid; idx < GS * HD; idx += kConsumerThreads) {
@@ -1007,7 +1018,8 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
         // incrementally; the ring size is a multiple of C)
         while (active && my_k < tile_end) {
             const int t = my_k - tile_base;
-            mbar_wait_bounded(bars + 8 * my_stage, my_phase, abort_flag, a.err, a.dbg, 2, my_k);
+            mbar_wait_bounded(bars + 8 * my_stage, my_phase, abort_flag, a.err, a.dbg, 2, my_k,
+                              true, wlim);
             const int nvalid = min(kTileRows, it.n - t * kTileRows);
             unsigned char* Kt = base + my_stage * 2 * G::TILEB;
             unsigned char* Vt = Kt + G::TILEB;

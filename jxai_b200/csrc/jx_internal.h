@@ -81,6 +81,9 @@ struct DecodeArgs {
     int q_bulk;              // 1: q rows and the rope table allow 16-byte bulk copies
                              // (the producer prefetches each piece's q into shared memory)
     int skip_append;         // 1: rows were appended by an earlier launch (prefill)
+    int test_wait_cta;       // > 0: CTA test_wait_cta-1 makes one bounded wait on a barrier
+                             // nothing arrives at (exercises the wait-timeout error path)
+    long long wait_limit;    // SM cycles after which a pipeline wait gives up
 };
 
 // Host-side launch request for one fused decode launch.
@@ -119,6 +122,8 @@ cudaError_t decode_launch(const DecodeLaunch& L);
 int consumers_for(int stages, int split);
 // Default ring depth and CTAs per SM for one kernel configuration.
 void default_shape(int hd, int gp, int kp, int dtype, int* stages, int* cps);
+// SM cycles of a bounded pipeline wait for a limit in milliseconds (0: default).
+long long wait_limit_cycles(int ms);
 // Sets the calling thread's jx_last_error_string() message.
 void set_last_error(const char* msg);
 // (cos, sin) of every rotated pair at `pos`, as apply_rope computes them;

@@ -351,6 +351,8 @@ struct jx_kv {
     int opt_pdl = -1;  // programmatic dependent launch: -1 auto, 0 off, 1 on
     int opt_timing = 0;  // 1: events around every step (jx_kv_last_step_ms)
     float opt_split_penalty_us = -1.0f;  // cost of an extra piece in a CTA's slice; -1: auto
+    int opt_wait_limit_ms = 0;   // bound of the kernel's pipeline waits; 0: the default (~4 s)
+    int opt_test_wait_cta = 0;   // test hook: CTA + 1 that waits on a barrier nothing arrives at
     cudaEvent_t ev_t0 = nullptr, ev_t1 = nullptr;
     bool timed = false;  // a timed step was recorded
     int last_launches = 0;
@@ -493,7 +495,7 @@ std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers
     put(k, a->sliding_window); put(k, a->yarn_scale); put(k, a->rope_neox);
     put(k, partials); put(k, stream);
     put(k, kv->opt_stages); put(k, kv->opt_ctas_per_sm); put(k, kv->opt_grid); put(k, kv->opt_pdl);
-    put(k, kv->opt_split_penalty_us);
+    put(k, kv->opt_split_penalty_us); put(k, kv->opt_wait_limit_ms); put(k, kv->opt_test_wait_cta);
     for (uint32_t s = 0; s < a->n_seqs; ++s) {
         put(k, a->pos[s]);
         put(k, a->seq_ids ? a->seq_ids[s] : -1);
@@ -507,6 +509,17 @@ std::vector<unsigned char> call_key(const jx_kv* kv, const jx_layer_desc* layers
     }
     return k;
 }
+
+}  // namespace
+
+// SM cycles of a bounded pipeline wait for a limit in milliseconds (counted at
+// 2 GHz, about B200's top SM clock, so a wait lasts at least that long); 0
+// selects the kernel's default of ~4 s.
+long long jx::wait_limit_cycles(int ms) {
+    return ms > 0 ? static_cast<long long>(ms) * 2000000ll : kWaitLimitCycles;
+}
+
+namespace {
 
 // Rows one CTA streams per microsecond when all P CTAs share HBM evenly
 // (~6.5 TB/s on B200): converts a per-piece time cost into rows.
@@ -950,6 +963,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                     reinterpret_cast<uintptr_t>(a->v) % 16 == 0 && a->kv_stride % 4 == 0)
                        ? 1 : 0;
         A.skip_append = prefill ? 1 : 0;
+        A.test_wait_cta = kv->opt_test_wait_cta;
+        A.wait_limit = wait_limit_cycles(kv->opt_wait_limit_ms);
         A.n_io = static_cast<long long>(a->n_seqs) * n_layers;
         A.cache_elems = kv->seq_stride * D.n_seqs;
         A.scratch_floats = static_cast<long long>(kv->scratch_floats);
@@ -1290,29 +1305,26 @@ int jx_kv_compact(jx_kv* kv, uint32_t seq, uint32_t keep_recent, void* stream) {
     const uint32_t src_start = sp - keep_recent;
     const size_t row_b = static_cast<size_t>(kv->d.row_stride) * kv->esz;
     const size_t layer_b = static_cast<size_t>(kv->layer_stride) * kv->esz;
-    const size_t width = static_cast<size_t>(keep_recent) * row_b;
     const size_t seq_off = static_cast<size_t>(seq) * kv->seq_stride * kv->esz;
     cudaStream_t st = (cudaStream_t)stream;
-    void* tmp = nullptr;
-    // Source and destination overlap (the reference uses memmove), so the
-    // kept rows go through a temporary buffer: one 2-D copy out, one back.
-    if (width > 0) {
-        if (cudaMalloc(&tmp, width * kv->d.n_layers) != cudaSuccess)
-            return fail(JX_ERR_NOMEM, "compaction buffer allocation failed");
+    // memmove of rows [src_start, src_start + keep) down to row `sink` in
+    // every layer (transformer.cpp:48-60).  Source and destination overlap when
+    // keep > src_start - sink, so the rows go in chunks of d = src_start - sink
+    // rows, front to back: chunk i reads rows that no earlier chunk writes and
+    // writes only rows chunk i-1 already read, and copies on one stream run in
+    // order -- memmove's result with no temporary buffer, no allocation and no
+    // host wait.  The reference's own trigger (keep = capacity/2 at seq_pos =
+    // capacity, :2373) takes two chunks per tensor.
+    const uint32_t d = src_start - sink;
+    for (uint32_t r = 0; r < keep_recent; r += d) {
+        const uint32_t n = std::min(d, keep_recent - r);
         for (int which = 0; which < 2; ++which) {
             char* basep = static_cast<char*>(which == 0 ? kv->k : kv->v) + seq_off;
-            cudaError_t e = cudaMemcpy2DAsync(tmp, width, basep + src_start * row_b, layer_b, width,
-                                              kv->d.n_layers, cudaMemcpyDeviceToDevice, st);
-            if (e == cudaSuccess)
-                e = cudaMemcpy2DAsync(basep + sink * row_b, layer_b, tmp, width, width,
-                                      kv->d.n_layers, cudaMemcpyDeviceToDevice, st);
-            if (e != cudaSuccess) {
-                cudaFree(tmp);
-                return fail(JX_ERR_CUDA, "compaction copy failed: %s", cudaGetErrorString(e));
-            }
+            JX_CUDA(cudaMemcpy2DAsync(basep + (sink + r) * row_b, layer_b,
+                                      basep + (src_start + r) * row_b, layer_b,
+                                      static_cast<size_t>(n) * row_b, kv->d.n_layers,
+                                      cudaMemcpyDeviceToDevice, st));
         }
-        JX_CUDA(cudaStreamSynchronize(st));
-        JX_CUDA(cudaFree(tmp));
     }
     kv->seq_pos[seq] = sink + keep_recent;
     return JX_OK;
@@ -1472,6 +1484,8 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
     else if (!std::strcmp(key, "timing")) kv->opt_timing = value ? 1 : 0;
     else if (!std::strcmp(key, "split_penalty_us"))
         kv->opt_split_penalty_us = value < 0 ? -1.0f : static_cast<float>(value);
+    else if (!std::strcmp(key, "wait_limit_ms")) kv->opt_wait_limit_ms = value;
+    else if (!std::strcmp(key, "test_wait_cta")) kv->opt_test_wait_cta = value;
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;
 }

@@ -26,7 +26,7 @@ def _torch():
 
 
 @pytest.mark.parametrize("dtype", [F16T, F32])
-@pytest.mark.parametrize("seq_pos,keep", [(64, 32), (40, 8), (10, 6), (37, 0), (64, 59)])
+@pytest.mark.parametrize("seq_pos,keep", [(64, 32), (40, 8), (10, 6), (37, 0), (64, 59), (61, 40)])
 def test_compact_matches_reference(dtype, seq_pos, keep):
     import jxai_b200 as jx
     rng = np.random.default_rng(seq_pos * 7 + keep)
