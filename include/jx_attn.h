@@ -47,7 +47,9 @@ enum {
     JX_ERR_UNSUPPORTED = -4, /* shape outside the compiled kernel set */
     JX_ERR_RANGE = -5,       /* position outside the cache (caller must compact first) */
     JX_ERR_DEVICE = -6,      /* a kernel reported a device-side error (bounded wait ran out) */
-    JX_ERR_TIMEOUT = -7,     /* a sharded step did not complete in time; communicator aborted */
+    JX_ERR_TIMEOUT = -7,     /* a sharded step did not complete in time (or a peer rank was
+                                not alive); its work stays queued and the communicator is
+                                untouched: whether to call ncclCommAbort is the caller's choice */
     JX_ERR_COMM = -8         /* an NCCL call failed or NCCL is not available */
 };
 
@@ -220,6 +222,21 @@ JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache, void* v_c
                                 const jx_layer_desc* layers, uint32_t n_layers,
                                 const jx_step_args* args, void* stream);
 
+/* Reads and clears the device error word of the no-allocation path on
+ * `device` (it synchronises `stream`).  No counterpart in the reference.  The
+ * word is shared by every jx_attn_step_noalloc call on that device and keeps
+ * the first error since it was last read: *code = 0 when no kernel reported
+ * one; otherwise *code is the kernel's error (1: a bounded wait ran out) and
+ * the call returns JX_ERR_DEVICE with the site in jx_last_error_string().
+ * Call it after the steps it covers have been queued, before relying on
+ * their outputs.  Allocates nothing. */
+JX_API int jx_noalloc_check_device_error(int device, int* code, void* stream);
+
+/* Options of the no-allocation path (it has no handle; they apply to every
+ * later jx_attn_step_noalloc call in the process): "wait_limit_ms" and
+ * "test_wait_cta" as in jx_kv_set_option.  No counterpart in the reference. */
+JX_API int jx_noalloc_set_option(const char* key, int value);
+
 /* ---- diagnostics, tuning, harness helpers --------------------------------- */
 
 /* Reads and clears the handle's device error word (synchronises the stream).
@@ -234,7 +251,12 @@ JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
  * jx_attn_step / jx_attn_step_partial (not while a stream is being captured);
  * "split_penalty_us" (-1 = default: 5 for fp32 caches, 8 for 16-bit; 0 =
  * uniform slices) is the time an extra piece costs a CTA, used to size the
- * CTAs' slices. */
+ * CTAs' slices; "wait_limit_ms" (0 = default, ~4 s) bounds every pipeline
+ * wait inside the kernel, after which the CTA gives up, sets the device error
+ * word and finishes (the step's output is then invalid);
+ * "test_wait_cta" N > 0 makes CTA N-1 of every launch wait once on a barrier
+ * nothing arrives at -- a test of that error path (use with a short
+ * "wait_limit_ms"; 0 = off). */
 JX_API int jx_kv_set_option(jx_kv* kv, const char* key, int value);
 
 /* Device time of the last step recorded with option "timing" (waits for it):

@@ -31,6 +31,7 @@ EXPORTS = (
     "jx_kv_check_device_error", "jx_kv_set_option", "jx_kv_last_launch_count",
     "jx_kv_fill_normal", "jx_fill_normal_f32", "jx_last_error_string", "jx_version",
     "jx_attn_step_noalloc", "jx_attn_step_sharded", "jx_kv_last_step_ms", "jx_attn_prefill",
+    "jx_noalloc_check_device_error", "jx_noalloc_set_option",
 )
 
 
@@ -92,6 +93,8 @@ def _declare(lib: C.CDLL) -> None:
         "jx_attn_step_sharded": [vp, C.POINTER(LayerDesc), u32, C.POINTER(StepArgs), vp, u32, vp],
         "jx_kv_last_step_ms": [vp, C.POINTER(C.c_float)],
         "jx_attn_prefill": [vp, C.POINTER(LayerDesc), u32, C.POINTER(StepArgs), vp],
+        "jx_noalloc_check_device_error": [C.c_int, C.POINTER(C.c_int), vp],
+        "jx_noalloc_set_option": [C.c_char_p, C.c_int],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

@@ -19,16 +19,26 @@
 //     (sequence, layer, kv head) segments fit; the 256-sequence ragged batch
 //     of the benchmark does not).
 //   * All calls share that one array and it keeps the last call's contents.
-//     Each call clears the part that must start at zero (counters and the
-//     device error words) on its own stream before its launch.  Calls that
+//     Each call clears the part that must start at zero (the per-segment
+//     arrival counters) on its own stream before its launch.  Calls that
 //     overlap on the GPU -- on different streams, or from different threads
 //     without ordering -- race on the array and give wrong results.
-//   * The first call on each device looks up the array's device address
-//     (cudaGetSymbolAddress) with that device current; make that first call
-//     before any stream capture.
+//   * A kernel that reports an error (a bounded wait that ran out) sets the
+//     device error word at the start of the array; it stays set until
+//     jx_noalloc_check_device_error reads and clears it, so one check after a
+//     run of steps reports the first error among them.
+//   * The first call on each device does its set-up: it looks up the array's
+//     device address (cudaGetSymbolAddress) with that device current and
+//     creates that device's plan-copy events; the first call in the process
+//     also page-locks the fixed host buffer the plan is built in
+//     (cudaHostRegister of the library's own static buffer -- no memory is
+//     allocated).  Make that first call before any stream capture.
 //   * Nothing here calls cudaMalloc, cudaFree, cudaMallocAsync, cudaHostAlloc
-//     or any other allocating routine: the work plan is built in a fixed host
-//     buffer (not on the heap) and copied into the array with cudaMemcpyAsync.
+//     or any other allocating routine: the work plan is built in one of four
+//     slots of the fixed host buffer (not on the heap) and copied into the
+//     array with cudaMemcpyAsync; a slot is reused only after the copy that
+//     last read it has run (its event), so the host runs up to four steps
+//     ahead of the GPU without waiting.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -36,6 +46,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "jx_attn.h"
@@ -46,7 +57,9 @@ namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // per GPU
 constexpr size_t kHeaderBytes = 256;                       // err word + dbg[8]
-constexpr size_t kPlanHostBytes = size_t(1) << 20;         // host staging for the plan
+constexpr int kPlanSlots = 4;                              // host plan buffers in flight
+constexpr size_t kPlanSlotBytes = size_t(1) << 20;         // one step's plan
+constexpr size_t kMaxPairs = kPlanSlotBytes / sizeof(jx::PairRow);
 constexpr int kMaxDevices = 64;
 
 // The scratch itself.  In host code `g_noalloc_scratch` is only a stand-in
@@ -54,9 +67,22 @@ constexpr int kMaxDevices = 64;
 // cudaGetSymbolAddress (per device) and is what the kernel receives.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-alignas(256) unsigned char g_plan_host[kPlanHostBytes];
+// Host side of the plan: kPlanSlots slots, page-locked once per process.
+alignas(4096) unsigned char g_plan_host[kPlanSlots * kPlanSlotBytes];
+struct RopeKey { uint32_t rdim, base, pos; const float* rf; };
+RopeKey g_rope_keys[kMaxPairs];        // plan building only (host)
 std::mutex g_mu;                       // one plan build / upload at a time
-unsigned char* g_dev_scratch[kMaxDevices] = {nullptr};
+bool g_plan_pinned = false;            // cudaHostRegister of g_plan_host succeeded
+bool g_pin_tried = false;
+int g_next_slot = 0;
+int g_slot_dev[kPlanSlots] = {-1, -1, -1, -1};  // device of each slot's last copy
+struct DeviceState {
+    unsigned char* scratch = nullptr;  // device address of g_noalloc_scratch
+    cudaEvent_t ev[kPlanSlots] = {};   // recorded after each slot's plan copy
+};
+DeviceState g_dev[kMaxDevices];
+std::atomic<int> g_opt_wait_limit_ms{0};
+std::atomic<int> g_opt_test_wait_cta{0};
 
 // Reports a failure through jx_last_error_string() (the calling thread's message).
 int nfail(int code, const char* fmt, ...) {
@@ -82,6 +108,62 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
     }
     return fn;
+}
+
+// Pointer check as jx_attn_step makes it: device memory of `dev` or (where
+// allowed) pinned host memory; pageable host memory or another device's
+// memory would fault the kernel.  An error this query raises is cleared only
+// when the caller had none pending, so a caller's unread error survives.
+int check_ptr(const void* p, const char* name, int dev, bool host_ok, bool* host) {
+    const cudaError_t pending = cudaPeekAtLastError();
+    cudaPointerAttributes at{};
+    const cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        if (pending == cudaSuccess) cudaGetLastError();
+        return nfail(JX_ERR_INVALID, "%s: not a CUDA-visible pointer (%s)", name,
+                     cudaGetErrorString(e));
+    }
+    if (at.type == cudaMemoryTypeHost && host_ok) {
+        *host = true;
+        return JX_OK;
+    }
+    *host = false;
+    if ((at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged) && at.device == dev)
+        return JX_OK;
+    return nfail(JX_ERR_INVALID, "%s must be memory of device %d%s", name, dev,
+                 host_ok ? " or pinned host memory" : "");
+}
+
+// Once per device (with it current): the scratch array's device address and
+// the plan-copy events; once per process: page-lock the host plan buffer.
+// Called with g_mu held.
+int setup_device(int dev) {
+    if (!g_pin_tried) {
+        g_pin_tried = true;
+        const cudaError_t pending = cudaPeekAtLastError();
+        g_plan_pinned = cudaHostRegister(g_plan_host, sizeof g_plan_host,
+                                         cudaHostRegisterPortable) == cudaSuccess;
+        // without it the copies still work, from pageable memory
+        if (!g_plan_pinned && pending == cudaSuccess) cudaGetLastError();
+    }
+    DeviceState& st = g_dev[dev];
+    if (st.scratch) return JX_OK;
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+        return nfail(JX_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
+    for (int i = 0; i < kPlanSlots; ++i)
+        if (!st.ev[i] && cudaEventCreateWithFlags(&st.ev[i], cudaEventDisableTiming) != cudaSuccess)
+            return nfail(JX_ERR_CUDA, "event creation failed");
+    st.scratch = static_cast<unsigned char*>(p);
+    return JX_OK;
+}
+
+int current_device(int want) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || dev != want)
+        return -1;
+    return dev;
 }
 
 }  // namespace
@@ -132,39 +214,51 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
                              "a shares-KV layer reads a cache layer appended in the same call; "
                              "split the call");
     }
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || dev != D.device)
+    const size_t n_pairs = static_cast<size_t>(a->n_seqs) * n_layers;
+    if (n_pairs > kMaxPairs)
+        return nfail(JX_ERR_RANGE, "step of %zu (sequence, layer) pairs exceeds the %zu the "
+                                   "no-allocation path plans", n_pairs, kMaxPairs);
+    const int dev = current_device(D.device);
+    if (dev < 0)
         return nfail(JX_ERR_INVALID, "make the cache's device (%d) current before the call",
                      D.device);
+    // the same pointer rules as jx_attn_step: inputs and output in this device's
+    // memory or pinned host memory, the caches in this device's memory
+    bool q_host = false, k_host = false, v_host = false, o_host = false, c_host = false;
+    int rc = check_ptr(a->q, "q", dev, true, &q_host);
+    if (!rc) rc = check_ptr(a->k, "k", dev, true, &k_host);
+    if (!rc) rc = check_ptr(a->v, "v", dev, true, &v_host);
+    if (!rc) rc = check_ptr(a->out, "out", dev, true, &o_host);
+    if (!rc) rc = check_ptr(k_cache, "k_cache", dev, false, &c_host);
+    if (!rc) rc = check_ptr(v_cache, "v_cache", dev, false, &c_host);
+    if (rc) return rc;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
     std::lock_guard<std::mutex> lk(g_mu);
-    // once per device: the device address of the static scratch array
-    if (!g_dev_scratch[dev]) {
-        void* p = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p)
-            return nfail(JX_ERR_CUDA, "cudaGetSymbolAddress(scratch) failed: %s",
-                         cudaGetErrorString(e));
-        g_dev_scratch[dev] = static_cast<unsigned char*>(p);
-    }
-    unsigned char* scratch = g_dev_scratch[dev];
+    rc = setup_device(dev);
+    if (rc) return rc;
+    unsigned char* scratch = g_dev[dev].scratch;
 
-    // ---- work plan, built in the fixed host buffer: pairs, then rope rows
-    const size_t n_pairs = static_cast<size_t>(a->n_seqs) * n_layers;
+    // ---- work plan, built in the next host slot: pairs, then rope rows.  The
+    // slot is reused only once the copy that last read it has run.
+    const int slot = g_next_slot;
+    if (g_slot_dev[slot] >= 0) {
+        const cudaError_t e = cudaEventSynchronize(g_dev[g_slot_dev[slot]].ev[slot]);
+        if (e != cudaSuccess)
+            return nfail(JX_ERR_CUDA, "plan slot wait failed: %s", cudaGetErrorString(e));
+        g_slot_dev[slot] = -1;
+    }
+    unsigned char* plan_host = g_plan_host + static_cast<size_t>(slot) * kPlanSlotBytes;
     const size_t pair_bytes = n_pairs * sizeof(PairRow);
     const size_t rope_off = round_up(pair_bytes, 256);
     const int width = static_cast<int>(hd / 2);
     const size_t row_bytes = static_cast<size_t>(width) * sizeof(float2);
-    if (rope_off + n_pairs * row_bytes > kPlanHostBytes)
+    if (rope_off + n_pairs * row_bytes > kPlanSlotBytes)
         return nfail(JX_ERR_RANGE, "step of %zu (sequence, layer) pairs exceeds the %zu-byte plan "
-                                   "buffer of the no-allocation path", n_pairs, kPlanHostBytes);
-    PairRow* pairs = reinterpret_cast<PairRow*>(g_plan_host);
-    float2* rope = reinterpret_cast<float2*>(g_plan_host + rope_off);
-    struct RopeKey { uint32_t rdim, base, pos; const float* rf; };
-    RopeKey* keys = reinterpret_cast<RopeKey*>(g_plan_host + kPlanHostBytes) - n_pairs;
-    if (reinterpret_cast<unsigned char*>(keys) < g_plan_host + rope_off + n_pairs * row_bytes)
-        return nfail(JX_ERR_RANGE, "step too large for the no-allocation plan buffer");
+                                   "slot of the no-allocation path", n_pairs, kPlanSlotBytes);
+    PairRow* pairs = reinterpret_cast<PairRow*>(plan_host);
+    float2* rope = reinterpret_cast<float2*>(plan_host + rope_off);
+    RopeKey* keys = g_rope_keys;
     int n_rope = 0;
     long long off = 0;
     const bool neox = a->rope_neox != 0;
@@ -263,12 +357,16 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
         if (r != CUDA_SUCCESS) return nfail(JX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     }
 
-    // ---- clear what must start at zero, upload the plan, launch
-    cudaError_t e = cudaMemsetAsync(scratch, 0, partials_off, stream);
+    // ---- clear the counters (the error word stays until it is read), upload
+    // the plan from its slot, launch
+    cudaError_t e = cudaMemsetAsync(scratch + counters_off, 0, partials_off - counters_off, stream);
     if (e == cudaSuccess)
-        e = cudaMemcpyAsync(scratch + plan_off, g_plan_host, plan_bytes, cudaMemcpyHostToDevice,
+        e = cudaMemcpyAsync(scratch + plan_off, plan_host, plan_bytes, cudaMemcpyHostToDevice,
                             stream);
+    if (e == cudaSuccess) e = cudaEventRecord(g_dev[dev].ev[slot], stream);
     if (e != cudaSuccess) return nfail(JX_ERR_CUDA, "scratch set-up failed: %s", cudaGetErrorString(e));
+    g_slot_dev[slot] = dev;
+    g_next_slot = (slot + 1) % kPlanSlots;
 
     DecodeLaunch Lc{};
     DecodeArgs& A = Lc.args;
@@ -301,22 +399,14 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     A.dbg = reinterpret_cast<int*>(scratch) + 8;
     A.n_stages = stages;
     A.n_consumers = consumers_for(stages, kp);
-    {
-        // q and the appended k/v rows are bulk-prefetched from device memory
-        // with 16-byte rows; otherwise they are read with ordinary loads
-        auto on_device = [](const void* p) {
-            cudaPointerAttributes at{};
-            const bool dev = cudaPointerGetAttributes(&at, p) == cudaSuccess &&
-                             at.type == cudaMemoryTypeDevice;
-            cudaGetLastError();
-            return dev;
-        };
-        A.q_bulk = (on_device(a->q) && on_device(a->k) && on_device(a->v) &&
-                    reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0 &&
-                    reinterpret_cast<uintptr_t>(a->k) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(a->v) % 16 == 0 && a->kv_stride % 4 == 0)
-                       ? 1 : 0;
-    }
+    // q and the appended k/v rows are bulk-prefetched from device memory with
+    // 16-byte rows; host-resident (pinned) inputs are read with ordinary loads
+    A.q_bulk = (!q_host && !k_host && !v_host && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 &&
+                a->q_stride % 4 == 0 && reinterpret_cast<uintptr_t>(a->k) % 16 == 0 &&
+                reinterpret_cast<uintptr_t>(a->v) % 16 == 0 && a->kv_stride % 4 == 0)
+                   ? 1 : 0;
+    A.test_wait_cta = g_opt_test_wait_cta.load();
+    A.wait_limit = wait_limit_cycles(g_opt_wait_limit_ms.load());
     A.n_io = static_cast<long long>(n_pairs);
     A.cache_elems = A.seq_stride * D.n_seqs;
     A.scratch_floats = static_cast<long long>(partial_floats);
@@ -338,5 +428,50 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     Lc.stream = stream;
     e = decode_launch(Lc);
     if (e != cudaSuccess) return nfail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
+    return JX_OK;
+}
+
+// Reads and clears the error word and the record of where the first error
+// happened (header of the scratch array), in stream order after the steps
+// queued on `stream`.
+extern "C" JX_API int jx_noalloc_check_device_error(int device, int* code, void* stream_ptr) {
+    if (!code) return nfail(JX_ERR_INVALID, "null code");
+    *code = 0;
+    const int dev = current_device(device);
+    if (dev < 0) return nfail(JX_ERR_INVALID, "make device %d current before the call", device);
+    cudaStream_t st = static_cast<cudaStream_t>(stream_ptr);
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = setup_device(dev);
+    if (rc) return rc;
+    unsigned char* scratch = g_dev[dev].scratch;
+    int hdr[16] = {0};  // err word, padding, dbg[8] at int offset 8
+    cudaError_t e = cudaMemcpyAsync(hdr, scratch, sizeof hdr, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && hdr[0] != 0) {
+        e = cudaMemsetAsync(scratch, 0, kHeaderBytes, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    }
+    if (e != cudaSuccess) return nfail(JX_ERR_CUDA, "error word read failed: %s", cudaGetErrorString(e));
+    *code = hdr[0];
+    const int* dbg = hdr + 8;
+    const long long v = static_cast<long long>(
+        (static_cast<uint64_t>(static_cast<uint32_t>(dbg[4])) << 32) | static_cast<uint32_t>(dbg[3]));
+    if (hdr[0] == kDevErrWaitTimeout)
+        return nfail(JX_ERR_DEVICE,
+                     "a no-allocation step's bounded wait ran out: site %d block %d thread %d "
+                     "tile %d after %lld cycles",
+                     dbg[0] - 100, dbg[1], dbg[2], dbg[5], v);
+    if (hdr[0])
+        return nfail(JX_ERR_DEVICE, "device check %d failed in block %d thread %d (error %d)",
+                     dbg[0], dbg[1], dbg[2], hdr[0]);
+    return JX_OK;
+}
+
+extern "C" JX_API int jx_noalloc_set_option(const char* key, int value) {
+    if (!key) return nfail(JX_ERR_INVALID, "null option");
+    if (value < 0) return nfail(JX_ERR_INVALID, "option '%s' takes a non-negative value", key);
+    if (!std::strcmp(key, "wait_limit_ms")) g_opt_wait_limit_ms = value;
+    else if (!std::strcmp(key, "test_wait_cta")) g_opt_test_wait_cta = value;
+    else return nfail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;
 }

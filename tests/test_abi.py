@@ -75,6 +75,11 @@ def test_invalid_arguments_rejected_on_host():
     assert lib.jx_lse_merge(None, 0, 0, 0, 0, 0, None, 0, None) == _lib.JX_ERR_INVALID
     assert lib.jx_attn_step_sharded(None, None, 0, None, None, 0, None) == _lib.JX_ERR_INVALID
     assert b"communicator" in lib.jx_last_error_string()
+    assert lib.jx_noalloc_check_device_error(0, None, None) == _lib.JX_ERR_INVALID
+    assert lib.jx_noalloc_set_option(b"no_such_option", 1) == _lib.JX_ERR_INVALID
+    assert lib.jx_noalloc_set_option(b"wait_limit_ms", -1) == _lib.JX_ERR_INVALID
+    assert lib.jx_noalloc_set_option(b"wait_limit_ms", 0) == _lib.JX_OK
+    assert lib.jx_noalloc_set_option(b"test_wait_cta", 0) == _lib.JX_OK
 
 
 def test_no_gpu_means_a_loud_failure():
