@@ -3,8 +3,11 @@
 
 One step = RoPE + KV append + grouped-query decode attention on every layer of
 every sequence of the workload (jxai src/transformer.cpp:2497-2566).  The
-default workload is Llama-3.2-1B shape (16 layers, 32/8 heads, head_dim 64)
-with an fp32 cache of 4095 rows, appending row 4095.
+default workload is c4, the long-context config the scaling target names:
+Mistral-7B shape (32 layers, 32/8 heads, head_dim 128) with one fp32 cache of
+131071 rows, appending row 131071 -- on one GPU the whole step, on N GPUs
+sharded by position.  --config c2 is BASELINE configs[1] (Llama-3.2-1B,
+T = 4096).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c1..c5] [--dtype f32|bf16]
     python bench.py --impl reference ...   # the reference's CPU implementation
@@ -39,10 +42,11 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--steps", type=int, default=None,
+                   help="timed steps (default: 2000 for c1/c2, 200 for the larger configs)")
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--config", default="c2")
+    p.add_argument("--config", default="c4")
     p.add_argument("--dtype", default=None, help="KV cache type (f32 | bf16 | f16)")
     p.add_argument("--cpu-sample-s", type=float, default=8.0,
                    help="seconds of CPU work for the cpu_baseline sample")
@@ -52,6 +56,9 @@ def parse_args():
                    help="untimed seconds of steps before warm-up so clocks leave idle")
     p.add_argument("--seqs", type=int, default=0,
                    help="keep only the first N sequences of the workload (small profiling cases)")
+    p.add_argument("--len", type=int, default=0, dest="length",
+                   help="attended length T of every sequence instead of the config's\n"
+                        "(small profiling cases of the long configs)")
     p.add_argument("--no-graph", action="store_true",
                    help="time K eager launches instead of one CUDA graph of K launches")
     p.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
@@ -64,7 +71,20 @@ def parse_args():
     p.add_argument("--prefill", type=int, default=0, metavar="N",
                    help="prompt throughput: one prompt of N tokens per jx_attn_prefill call\n"
                         "(full-attention configs), the reference's token-serial loop beside it")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.steps is None:
+        a.steps = 2000 if a.config.lower() in ("c1", "c2", "qwen2.5-0.5b", "llama-3.2-1b") else 200
+    return a
+
+
+def make_workload(args) -> W.Workload:
+    """The config's workload, cut to --seqs sequences / --len rows if asked."""
+    w = W.make(args.config, args.dtype)
+    if args.seqs > 0:
+        w.lengths = w.lengths[:args.seqs]
+    if args.length > 0:
+        w.lengths = [args.length] * len(w.lengths)
+    return w
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -156,9 +176,14 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- our arm
 
 class Runner:
-    """One rank's share of a workload, driven through the public Python API."""
+    """One rank's share of a workload, driven through the public Python API.
 
-    def __init__(self, w: W.Workload, rank: int, world: int, device: int, options=()):
+    extra_rows: cache rows beyond the workload's lengths, for steps that go on
+    decoding (each appends one more row); in a position-sharded run they go to
+    the last shard, which holds the newest positions."""
+
+    def __init__(self, w: W.Workload, rank: int, world: int, device: int, options=(),
+                 extra_rows: int = 0):
         import torch
         import jxai_b200 as jx
         self.torch, self.jx, self.w = torch, jx, w
@@ -172,10 +197,11 @@ class Runner:
         self.pos_base = 0
         if self.mode == "positions":
             (b, e) = W.position_shards(T[0], world)[rank]
-            self.pos_base, cap = b, e - b
+            self.shard = (b, e)
+            self.pos_base, cap = b, e - b + (extra_rows if rank == world - 1 else 0)
             rows = [max(0, min(e, T[0] - 1) - b)]
         else:
-            cap = max(self.local)
+            cap = max(self.local) + extra_rows
             rows = [t - 1 for t in self.local]
         n = len(self.local)
         self.n = n
@@ -197,28 +223,26 @@ class Runner:
             hd2 = w.head_dim + 2
             self.partials = torch.empty(n * w.n_layers * w.n_heads * hd2, device=dev)
             self.gathered = torch.empty(world * self.partials.numel(), device=dev)
-        # KV bytes this rank reads per step
-        if self.mode == "positions":
-            (b, e) = W.position_shards(T[0], world)[rank]
-            rows_att = sum(max(0, min(e, T[0]) - max(b, T[0] - w.attended(T[0], L)))
-                           for L in w.layers)
-            self.kv_bytes = rows_att * w.kv_dim * 2 * w.elem_size
-        else:
-            self.kv_bytes = w.kv_read_bytes(self.local)
+        self.kv_bytes = self.kv_bytes_at(0)  # KV bytes this rank reads per step
         self.alg_bytes = self.kv_bytes + w.other_bytes(n)
         self._plan = self.plan()
 
-    def plan(self, q=None, k=None, v=None, out=None):
-        """The step's C call with its arguments built once (jx.StepPlan)."""
+    def kv_bytes_at(self, shift: int = 0) -> int:
+        """KV bytes this rank reads in a step `shift` tokens after the first."""
+        return W.rank_kv_bytes(self.w, self.mode, self.rank, self.world, shift)
+
+    def plan(self, q=None, k=None, v=None, out=None, comm=None):
+        """The step's C call with its arguments built once (jx.StepPlan); with
+        `comm` (an ncclComm_t) the library's whole sharded step."""
         q = self.q if q is None else q
         k = self.k if k is None else k
         v = self.v if v is None else v
         out = self.out if out is None else out
         w = self.w
+        partials = self.partials if (self.mode == "positions" and comm is None) else None
         return self.jx.StepPlan(self.cache, w.layers, q, k, v, out, self.pos, w.n_heads,
                                 w.n_kv_heads, scale=w.scale, sliding_window=w.window,
-                                neox=w.neox,
-                                partials=self.partials if self.mode == "positions" else None)
+                                neox=w.neox, partials=partials, comm=comm)
 
     def kernel(self, plan=None):
         (plan or self._plan).run()
@@ -249,10 +273,10 @@ def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(local_rank)
-    w = W.make(args.config, args.dtype)
-    if args.seqs > 0:
-        w.lengths = w.lengths[:args.seqs]
-    r = Runner(w, rank, world, local_rank, args.set)
+    w = make_workload(args)
+    # the end-to-end leg decodes warmup + K further tokens: room for their rows
+    extra = 0 if args.no_e2e else args.warmup + args.steps
+    r = Runner(w, rank, world, local_rank, args.set, extra_rows=extra)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -357,14 +381,19 @@ def run_ours(args, rank, world, local_rank):
     clocks = sampler.summary(t_wall0, t_wall1)
     sampler.stop()
 
-    # ---- end to end through the public API with host buffers
+    # ---- end to end through the public API with host buffers, decoding on:
+    # every step is the next token of every sequence (pos + 1, as forward_token
+    # advances seq_pos, src/transformer.cpp:2792), so each call builds a new
+    # plan and RoPE rows and appends a new row, and attends one row more.
     e2e = None
+    comm = None
     if not args.no_e2e:
         # q, k, v and the output in pinned host memory.  Sharded-position
-        # steps (a collective) stage them: one H2D copy of q|k|v and one D2H
-        # copy of the output per step.  Otherwise the C ABI call takes the host
-        # buffers themselves: the library copies q/k/v into device memory with
-        # one staging kernel and the decode kernel writes attn_out over PCIe.
+        # steps stage them: one H2D copy of q|k|v and one D2H copy of the
+        # output per step around jx_attn_step_sharded (partial step, NCCL
+        # all-gather, merge).  Otherwise the C ABI call takes the host buffers
+        # themselves: the library copies q/k/v into device memory with one
+        # staging kernel and the decode kernel writes attn_out over PCIe.
         nq, nk = r.q.numel(), r.k.numel()
         inh = torch.empty(nq + 2 * nk, pin_memory=True)
         inh[:nq].copy_(r.q.reshape(-1).cpu())
@@ -376,24 +405,29 @@ def run_ours(args, rank, world, local_rank):
         if zero_copy:
             e2e_plan = r.plan(qh.view(r.q.shape), kh.view(r.k.shape), vh.view(r.v.shape), oh)
 
-            def e2e_step():
-                r.kernel(e2e_plan)
+            def e2e_step(i):
+                e2e_plan.set_positions([p + i for p in r.pos])
+                e2e_plan.run()
         else:
+            from jxai_b200.nccl import NcclComm
+            uid = [NcclComm.unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            comm = NcclComm(world, rank, uid[0])
             ind = torch.empty(nq + 2 * nk, device=r.q.device)
             qd = ind[:nq].view(r.q.shape)
             kd = ind[nq:nq + nk].view(r.k.shape)
             vd = ind[nq + nk:].view(r.v.shape)
             od = torch.empty_like(r.out)
-            e2e_plan = r.plan(qd, kd, vd, od)
+            e2e_plan = r.plan(qd, kd, vd, od, comm=comm.handle)
 
-            def e2e_step():
+            def e2e_step(i):
                 ind.copy_(inh, non_blocking=True)
-                r.kernel(e2e_plan)
-                r.finish(od)
+                e2e_plan.set_positions([p + i for p in r.pos])
+                e2e_plan.run()
                 oh.copy_(od, non_blocking=True)
 
-        for _ in range(args.warmup):
-            e2e_step()
+        for i in range(args.warmup):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
@@ -401,23 +435,32 @@ def run_ours(args, rank, world, local_rank):
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
         h0 = time.perf_counter()
-        for _ in range(K):
-            e2e_step()
+        for i in range(args.warmup, args.warmup + K):
+            e2e_step(i)
         host_ms = (time.perf_counter() - h0) * 1e3 / K
         b.record(stream)
         torch.cuda.synchronize()
         barrier()
+        if r.cache.check_device_error():
+            raise RuntimeError("device error during the end-to-end steps")
         e2e_ms = max_over_ranks(a.elapsed_time(b))
+        e2e_kv = sum_over_ranks(sum(r.kv_bytes_at(i) for i in range(args.warmup,
+                                                                     args.warmup + K)))
         h2d = sum_over_ranks((qh.numel() + kh.numel() + vh.numel()) * 4)
         d2h = sum_over_ranks(oh.numel() * 4)
-        e2e = {"value": round(total_kv * K / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+        e2e = {"value": round(e2e_kv / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h),
                "host_issue_ms_per_step": round(host_ms, 5),
+               "positions": f"advancing: step i appends row T-1+i and attends T+i rows "
+                            f"(i = {args.warmup}..{args.warmup + K - 1} timed)",
                "path": ("pinned host q|k|v and attn_out passed to jx_attn_step (C ABI); the "
                         "library copies q|k|v to device memory with one staging kernel and "
                         "the decode kernel writes attn_out over PCIe" if zero_copy else
-                        "pinned host q|k|v -> one H2D -> jx_attn_step (C ABI) -> one D2H attn_out")}
+                        "pinned host q|k|v -> one H2D -> jx_attn_step_sharded (C ABI: partial "
+                        "step, ncclAllGather, merge) -> one D2H attn_out")}
+        if comm is not None:
+            comm.destroy()
 
     # ---- CPU baseline (rank 0, N=1)
     cpu = None
@@ -431,13 +474,15 @@ def run_ours(args, rank, world, local_rank):
     traffic = ncu_traffic(f"{w.name}/{w.dtype}") if world == 1 else None
     steps_per_s = K / (elapsed_ms * 1e-3)
     value = total_kv * K / (elapsed_ms * 1e-3) / 1e9
-    parallel = {"replica": f"replicas x{world}", "sequences": f"sequences split over {world} GPUs (LPT)",
-                "positions": f"positions sharded over {world} GPUs + NCCL all-gather"}[r.mode]
+    parallel = ("one GPU" if world == 1 else
+                {"replica": f"replicas x{world}",
+                 "sequences": f"sequences split over {world} GPUs (LPT)",
+                 "positions": f"positions sharded over {world} GPUs + NCCL all-gather"}[r.mode])
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": round(elapsed_ms / K, 5),
         "steps_per_s": round(steps_per_s, 2), "higher_is_better": True,
-        "scaling": "weak" if r.mode in ("replica",) else "strong",
+        "scaling": "weak" if w.sharding == "replica" else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), device-side)",
         "config": dict(w.describe(), parallelism=parallel,
                        l2=("inputs larger than L2: %.0f MB of KV per step per GPU > 126 MB" %
@@ -538,9 +583,7 @@ def run_reference(args, rank, world):
     """The reference's own CPU implementation of the step on this host's cores."""
     if rank != 0:
         return
-    w = W.make(args.config, args.dtype)
-    if args.seqs > 0:
-        w.lengths = w.lengths[:args.seqs]
+    w = make_workload(args)
     orc, kind = _cpu_oracle(all_threads=True)
     n_seqs, n_layers, kv_bytes = _cpu_sample_shape(w)
     rng = np.random.default_rng(W.SEED)
@@ -769,7 +812,11 @@ def main():
     import torch
     import torch.distributed as dist
     if world > 1:
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
+        # NCCL's communicator lines (rank, nranks, transports) go to stderr:
+        # stdout keeps the one JSON line
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),

@@ -341,8 +341,13 @@ def attn_step_sharded(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos
     `comm` (an ncclComm_t address, e.g. NcclComm.handle) and merges them into
     `out` on every rank.  timeout_ms > 0 also waits for completion and raises
     JxError code -7 when the step does not finish in time (the communicator
-    is left to the caller to abort).
+    is left to the caller to abort).  With `heartbeat` (a
+    jxai_b200.liveness.Heartbeat) every rank first announces `step` and waits
+    up to liveness_timeout_s for the others: a rank that left raises JxError
+    code -7 here, before anything of the step is queued.
     """
+    if heartbeat is not None:
+        heartbeat.check(step, liveness_timeout_s)
     arr, keep = _layer_array(layers)
     a, keep2 = _step_args(cache, layers, q, k, v, out, pos, n_heads, n_kv_heads, scale, softcap,
                           sliding_window, yarn_scale, neox, seq_ids, 0)
@@ -352,26 +357,37 @@ def attn_step_sharded(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos
 
 
 class StepPlan:
-    """One attn_step (or attn_step_partial) call with its C arguments built once.
+    """One attn_step (or attn_step_partial, or attn_step_sharded) call with its
+    C arguments built once.
 
-    For callers that repeat the same step on the same buffers (a decode loop
-    whose inputs are rewritten in place, or a benchmark): run() costs one
-    foreign call.  The library additionally recognises an identical call and
-    relaunches the launches it built for it.
+    For callers that repeat the step on the same buffers (a decode loop whose
+    inputs are rewritten in place, or a benchmark): run() costs one foreign
+    call, and set_positions() moves every sequence to its next position.  The
+    library additionally recognises an identical call and relaunches the
+    launches it built for it.  With `comm` (an ncclComm_t address) the call is
+    jx_attn_step_sharded over that communicator.
     """
 
     def __init__(self, cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos: Sequence[int],
                  n_heads: int, n_kv_heads: int, scale: Optional[float] = None,
                  softcap: float = 0.0, sliding_window: int = 0, yarn_scale: float = 1.0,
-                 neox: bool = True, seq_ids: Optional[Sequence[int]] = None, partials=None):
+                 neox: bool = True, seq_ids: Optional[Sequence[int]] = None, partials=None,
+                 comm=None, timeout_ms: int = 0):
         self.cache = cache
         self.arr, self._keep = _layer_array(layers)
         self.args, self._keep2 = _step_args(cache, layers, q, k, v, out if partials is None else None,
                                             pos, n_heads, n_kv_heads, scale, softcap,
                                             sliding_window, yarn_scale, neox, seq_ids, 0)
         self._tensors = (q, k, v, out, partials)
+        self._pos = self._keep2[0]  # the ctypes position array args.pos points at
         self.n_layers = len(layers)
-        if partials is None:
+        if comm is not None:
+            if partials is not None:
+                raise JxError(-1, "a sharded step writes out, not partials")
+            self._call = cache.lib.jx_attn_step_sharded
+            self._head = (cache.handle, self.arr, self.n_layers, C.byref(self.args),
+                          C.c_void_p(int(comm)), int(timeout_ms))
+        elif partials is None:
             self._call = cache.lib.jx_attn_step
             self._head = (cache.handle, self.arr, self.n_layers, C.byref(self.args))
         else:
@@ -379,6 +395,15 @@ class StepPlan:
             pp = _dev_ptr(partials, "partials", len(pos) * len(layers) * n_heads * (hd + 2))
             self._call = cache.lib.jx_attn_step_partial
             self._head = (cache.handle, self.arr, self.n_layers, C.byref(self.args), pp)
+
+    def set_positions(self, pos: Sequence[int]) -> None:
+        """New positions for the next run() (same sequences): a decode loop
+        advancing every slot by one token, as forward_token's seq_pos++
+        (src/transformer.cpp:2792).  The library then builds that step's plan."""
+        if len(pos) != len(self._pos):
+            raise JxError(-1, "set_positions: one position per sequence of the plan")
+        for i, p in enumerate(pos):
+            self._pos[i] = int(p)
 
     def run(self, stream=None) -> None:
         rc = self._call(*self._head, _stream_ptr(stream))

@@ -1416,8 +1416,30 @@ int jx_attn_step_sharded(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_laye
     rc = jx_attn_step_partial(kv, layers, n_layers, args, kv->d_part, stream);
     if (rc) return rc;
     const ncclResult_t r = nc.all_gather(kv->d_part, kv->d_gather, per, ncclFloat32, comm, st);
-    if (r != ncclSuccess)
+    if (r == ncclInProgress) {
+        // A non-blocking communicator (blocking = 0) may still be connecting:
+        // the all-gather is accepted and goes on in the background; no other
+        // NCCL call may be made on it until its state leaves ncclInProgress.
+        const uint32_t limit_ms = timeout_ms > 0 ? timeout_ms : 120000;
+        const auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            ncclResult_t ae = ncclInProgress;
+            if (nc.comm_get_async_error(comm, &ae) != ncclSuccess)
+                return fail(JX_ERR_COMM, "ncclCommGetAsyncError failed");
+            if (ae == ncclSuccess) break;
+            if (ae != ncclInProgress)
+                return fail(JX_ERR_COMM, "ncclAllGather: %s", nc.get_error_string(ae));
+            const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                                std::chrono::steady_clock::now() - t0).count();
+            if (ms > static_cast<long long>(limit_ms))
+                return fail(JX_ERR_TIMEOUT,
+                            "ncclAllGather still in progress after %u ms (a rank that never "
+                            "joined?)", limit_ms);
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+    } else if (r != ncclSuccess) {
         return fail(JX_ERR_COMM, "ncclAllGather: %s", nc.get_error_string(r));
+    }
     rc = jx_lse_merge(kv->d_gather, static_cast<uint32_t>(world), per, static_cast<uint32_t>(groups),
                       args->n_heads, hd, args->out, static_cast<uint32_t>(args->q_stride), stream);
     if (rc) return rc;

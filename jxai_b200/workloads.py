@@ -137,3 +137,23 @@ def lpt_partition(lengths: Sequence[int], n_parts: int, cost=None) -> List[List[
 def position_shards(T: int, n_parts: int) -> List[tuple]:
     """Contiguous position ranges [begin, end) of one long sequence, one per rank."""
     return [(T * r // n_parts, T * (r + 1) // n_parts) for r in range(n_parts)]
+
+
+def rank_kv_bytes(w: Workload, mode: str, rank: int, world: int, shift: int = 0) -> int:
+    """KV bytes one rank reads in a step `shift` tokens after the workload's
+    first (every sequence then one row longer).  mode: "replica" (every rank
+    the whole workload), "sequences" (the LPT share of the sequences) or
+    "positions" (one sequence sharded by position; rows past the first step's
+    shard ends belong to the last rank, which holds the newest positions)."""
+    if mode == "positions":
+        T0 = w.lengths[0]
+        T = T0 + shift
+        b, e = position_shards(T0, world)[rank]
+        end = T if rank == world - 1 else min(e, T)
+        rows = sum(max(0, end - max(b, T - w.attended(T, L))) for L in w.layers)
+        return rows * w.kv_dim * 2 * w.elem_size
+    if mode == "sequences":
+        local = [w.lengths[i] for i in lpt_partition(w.lengths, world)[rank]]
+    else:
+        local = list(w.lengths)
+    return w.kv_read_bytes([t + shift for t in local])

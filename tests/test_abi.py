@@ -107,3 +107,37 @@ def test_cmake_project_configures():
         r = subprocess.run([cmake, "-S", root, "-B", td, f"-DCMAKE_CUDA_COMPILER={nvcc}"],
                            capture_output=True, text=True)
         assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_nccl_config_mirror_matches_the_header():
+    # jxai_b200.nccl builds ncclConfig_t through ctypes for the non-blocking
+    # communicator creation: same size and offsets as the header of the NCCL
+    # the process loads (torch's copy)
+    import glob
+    from jxai_b200.nccl import _Config
+    heads = glob.glob(os.path.join(os.path.dirname(os.__file__), "..", "..", "lib", "python3*",
+                                   "site-packages", "nvidia", "nccl", "include", "nccl.h"))
+    try:
+        import nvidia.nccl
+        heads += glob.glob(os.path.join(list(nvidia.nccl.__path__)[0], "include", "nccl.h"))
+    except ImportError:
+        pass
+    if not heads:
+        pytest.skip("NCCL header not found")
+    fields = [name for name, _ in _Config._fields_]
+    src = "#include <stdio.h>\n#include <stddef.h>\n#include \"nccl.h\"\nint main(void){\n"
+    src += 'printf("%zu\\n", sizeof(ncclConfig_t));\n'
+    src += "".join(f'printf("%zu\\n", offsetof(ncclConfig_t, {f}));\n' for f in fields)
+    src += "return 0;}\n"
+    with tempfile.TemporaryDirectory() as d:
+        c = os.path.join(d, "t.c")
+        exe = os.path.join(d, "t")
+        with open(c, "w") as fh:
+            fh.write(src)
+        cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+        subprocess.run(["gcc", "-I", os.path.dirname(heads[0]), "-I", cuda_inc, c, "-o", exe],
+                       check=True)
+        vals = [int(x) for x in subprocess.run([exe], capture_output=True, text=True,
+                                               check=True).stdout.split()]
+    assert vals[0] == C.sizeof(_Config)
+    assert vals[1:] == [getattr(_Config, f).offset for f in fields]

@@ -15,7 +15,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _check_line(d, n_gpus):
+def _check_line(d, n_gpus, workload):
     for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
                 "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
                 "cpu_baseline", "e2e"):
@@ -23,7 +23,7 @@ def _check_line(d, n_gpus):
     assert d["impl"] == "reference"
     assert d["metric"] == "decode-attn KV-read HBM GB/s" and d["unit"] == "GB/s"
     assert d["value"] > 0 and d["higher_is_better"] is True and d["n_gpus"] == n_gpus
-    assert d["config"]["workload"] == "c2"
+    assert d["config"]["workload"] == workload
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1
     assert cb["sample"]
@@ -37,13 +37,14 @@ def _json_lines(out):
 
 
 def test_reference_arm_prints_one_json_line():
+    # the default workload: c4, one layer of the 131072-row context per step
     r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
                         "--steps", "2", "--warmup", "3"],
                        capture_output=True, text=True, timeout=300, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = _json_lines(r.stdout)
     assert len(lines) == 1
-    _check_line(lines[0], 1)
+    _check_line(lines[0], 1, "c4")
 
 
 def test_reference_arm_under_torchrun_rank0_only():
@@ -52,7 +53,7 @@ def test_reference_arm_under_torchrun_rank0_only():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", "29561",
            os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2", "--steps", "2",
-           "--warmup", "3"]
+           "--warmup", "3", "--config", "c2"]
     try:
         r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT)
     except subprocess.TimeoutExpired:
@@ -60,5 +61,5 @@ def test_reference_arm_under_torchrun_rank0_only():
     assert r.returncode == 0, r.stderr[-2000:]
     lines = _json_lines(r.stdout)
     assert len(lines) == 1
-    _check_line(lines[0], 2)
+    _check_line(lines[0], 2, "c2")
     assert lines[0]["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))

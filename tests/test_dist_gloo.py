@@ -106,3 +106,64 @@ def test_sharded_host_logic_two_ranks(world):
     for rank, ok_seq, err in res:
         assert ok_seq
         assert err < 1e-5, err
+
+
+def _liveness_worker(rank, world, port, q):
+    # rank 1 runs step 0 and then leaves (its process ends between steps);
+    # rank 0's next liveness check must raise JX_ERR_TIMEOUT before anything
+    # of step 1 is queued
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=timedelta(seconds=30))
+    from jxai_b200 import JxError
+    from jxai_b200._lib import JX_ERR_TIMEOUT
+    from jxai_b200.liveness import Heartbeat
+    hb = Heartbeat(store, rank, world)
+    queued = []
+    res = {"rank": rank}
+    try:
+        hb.check(0, timeout_s=20.0)  # both ranks are alive for step 0
+        queued.append(0)             # stands for the sharded step's launch
+        if rank == 1:
+            q.put(res)
+            return                   # leaves between steps
+        import time
+        t0 = time.monotonic()
+        try:
+            hb.check(1, timeout_s=1.0)
+            queued.append(1)
+            res["raised"] = None
+        except JxError as e:
+            res["raised"] = e.code
+            res["msg"] = str(e)
+        res["elapsed"] = time.monotonic() - t0
+        res["queued"] = queued
+        res["code"] = JX_ERR_TIMEOUT
+    except Exception as ex:  # reported to the parent
+        res["exc"] = repr(ex)
+    q.put(res)
+    if rank == 0:
+        import time
+        time.sleep(0.5)  # the store server outlives the other rank's last read
+
+
+def test_liveness_check_reports_a_rank_that_left():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_liveness_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        r = q.get(timeout=120)
+        res[r["rank"]] = r
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert "exc" not in res[0] and "exc" not in res[1], res
+    r0 = res[0]
+    assert r0["raised"] == r0["code"], r0
+    assert "[1]" in r0["msg"] and "step 1" in r0["msg"]
+    assert r0["queued"] == [0]          # step 1 queued nothing
+    assert 0.9 <= r0["elapsed"] < 10.0  # the deadline, not the store's 30 s timeout

@@ -47,7 +47,9 @@ def _worker(rank, world, q_uid, q_res):
                 q_uid.put(uid)
         else:
             uid = q_uid.get(timeout=120)
-        comm = NcclComm(world, rank, uid)
+        # non-blocking creation with a deadline (the all-gather may then report
+        # ncclInProgress while the communicator connects; the library waits)
+        comm = NcclComm(world, rank, uid, timeout_s=120)
         kc, vc, q, k, v = _case()
         rs = HK * HD
         b, e = T * rank // world, T * (rank + 1) // world
@@ -111,3 +113,45 @@ def test_sharded_step_matches_unsharded_oracle():
         assert r["dev_err"] == 0
         assert r["err"] <= TOL, r
         assert r["append_ok"], r
+
+
+def _lonely_rank(q_res):
+    # rank 0 of a 2-rank communicator whose rank 1 never exists: the
+    # non-blocking creation must give up at its deadline (host side: NCCL's
+    # bootstrap waits for the peer; no kernel runs)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import time
+    import torch
+    torch.cuda.set_device(0)
+    from jxai_b200.nccl import NcclComm, NcclTimeout
+    res = {}
+    t0 = time.monotonic()
+    try:
+        NcclComm(2, 0, NcclComm.unique_id(), timeout_s=3.0)
+        res["raised"] = None
+    except NcclTimeout as e:
+        res["raised"] = "timeout"
+        res["msg"] = str(e)
+    except Exception as e:
+        res["raised"] = repr(e)
+    res["elapsed"] = time.monotonic() - t0
+    q_res.put(res)
+
+
+def test_nonblocking_init_gives_up_when_a_rank_never_joins():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 1:
+        pytest.skip("needs a GPU")
+    ctx = mp.get_context("spawn")
+    q_res = ctx.Queue()
+    p = ctx.Process(target=_lonely_rank, args=(q_res,))
+    p.start()
+    try:
+        res = q_res.get(timeout=180)
+    finally:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res["raised"] == "timeout", res
+    assert 2.9 <= res["elapsed"] < 60.0, res

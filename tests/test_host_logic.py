@@ -47,6 +47,19 @@ def test_position_shards_cover_the_sequence(n):
     assert max(e - b for b, e in sh) - min(e - b for b, e in sh) <= 1
 
 
+@pytest.mark.parametrize("name,mode", [("c4", "positions"), ("c3", "sequences"),
+                                       ("c5", "sequences"), ("c2", "replica")])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_rank_kv_bytes_add_up_to_the_step(name, mode, world):
+    # the ranks' shares of a step (the bench's value and its e2e leg, whose
+    # steps advance by one row each) add up to the whole step's KV bytes
+    w = W.make(name)
+    for shift in (0, 1, 7, 220):
+        total = sum(W.rank_kv_bytes(w, mode, r, world, shift) for r in range(world))
+        whole = w.kv_read_bytes([t + shift for t in w.lengths])
+        assert total == (whole * world if mode == "replica" else whole), (shift, total, whole)
+
+
 def test_slice_planner_boundaries_and_layout_forms(tmp_path):
     # jx::balanced_split (jxai_b200/csrc/jx_plan.h) sizes the persistent CTAs'
     # slices of a step; built with g++ alone and checked on seeded random
