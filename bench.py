@@ -715,6 +715,9 @@ def run_prefill(args, rank, world):
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     cache = jx.KVCache(1, w.n_layers, N, w.kv_dim, w.dtype, 0)
+    for opt in args.set:
+        key, _, val = opt.partition("=")
+        cache.set_option(key, int(val))
     q = torch.empty(N, w.n_layers, w.q_dim, device=dev)
     k = torch.empty(N, w.n_layers, w.kv_dim, device=dev)
     v = torch.empty_like(k)

@@ -28,7 +28,7 @@ LIB_CHECKED = os.path.join(PKG, "libjxattn_checked.so")
 STAMP_CHECKED = os.path.join(BUILD, "checked", "libjxattn.sources.sha256")
 
 SOURCES = ["jx_lib.cu", "jx_decode_f32.cu", "jx_decode_bf16.cu", "jx_decode_f16.cu",
-           "jx_noalloc.cu"]
+           "jx_noalloc.cu", "jx_prefill_tc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
          f"-I{INCLUDE}", f"-I{CSRC}"]

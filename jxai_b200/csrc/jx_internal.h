@@ -101,6 +101,45 @@ struct DecodeLaunch {
     cudaStream_t stream;
 };
 
+// One work item of the tensor-core prefill kernel: `ntok` consecutive prompt
+// tokens of one sequence (local cache rows tok_row0 ..), one layer, one kv
+// head.  Token j has q/out row io0 + j*io_step and cos/sin row rope_row0 + j,
+// and attends local rows [max(row0, tok_row0 + j - window + 1), tok_row0 + j]
+// (window 0: from row0).  The kernel streams cache rows [kv_lo, kv_lo +
+// n_tiles*BN) of the item.
+struct PrefillTile {
+    int seq, cache_layer, kvh, io0;
+    int io_step, tok_row0, ntok, row0;
+    int window, rope_row0, rope_half, kv_lo;
+    int n_tiles;
+    int pad[3];
+};
+static_assert(sizeof(PrefillTile) == 64, "PrefillTile layout");
+
+struct PrefillArgs {
+    const PrefillTile* tiles;
+    int n_items;
+    int neox;
+    const float* q;
+    float* out;
+    long long q_stride;
+    const float2* rope;  // rows of head_dim/2 (cos, sin) pairs
+    float scale;
+    float softcap;
+    float inv_softcap;
+    int* err;
+    int* dbg;
+    long long wait_limit;
+};
+
+// Tensor-core prefill for (head_dim, cache dtype, query group) -- 16-bit
+// caches, head_dim 64/128, groups 1/2/4/8; cache rows per K/V tile of the
+// kernel for a head_dim (the TMA box height); launch of one grid.
+bool prefill_tc_supported(int head_dim, int dtype, int G);
+int prefill_tc_rows(int head_dim);
+cudaError_t prefill_tc_launch(const PrefillArgs& a, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                              int head_dim, int dtype, int G, int grid, cudaStream_t stream);
+
 // kv heads that share one tile row: 2 for 16-bit caches whose kv-head rows
 // are under 256 bytes (head_dim 32, 64) when the heads pair up evenly and the
 // query group needs no padding, 1 otherwise.  With 2, each tile row the TMA

@@ -337,6 +337,11 @@ struct jx_kv {
     // tensor maps by TMA box inner extent: [0] = 128-byte boxes, [1] = 64-byte boxes
     CUtensorMap tmK[2], tmV[2];
     bool tm_ok[2] = {false, false};
+    // tensor maps of the tensor-core prefill (128-byte boxes, 128-byte swizzle) by box
+    // height: [0] = 128 rows (head_dim 64), [1] = 64 rows (head_dim 128)
+    CUtensorMap tmKp[2], tmVp[2];
+    bool tmp_ok[2] = {false, false};
+    int opt_prefill_tc = 1;  // 16-bit caches: prefill attention on the tensor cores (tcgen05)
     std::vector<uint32_t> seq_pos;
     int num_sms = 0;
     int* d_err = nullptr;
@@ -400,6 +405,33 @@ int encode_maps(jx_kv* kv, int box_kind) {
         if (r != CUDA_SUCCESS) return fail(JX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     }
     kv->tm_ok[box_kind] = true;
+    return JX_OK;
+}
+
+// Tensor maps of the tensor-core prefill: boxes of 64 16-bit elements (128
+// bytes, one head-row slab) x `rows` cache rows, 128-byte swizzle -- the
+// K-major / MN-major operand layout the kernel's MMAs read.
+int encode_prefill_maps(jx_kv* kv, int kind, int rows) {
+    if (kv->tmp_ok[kind]) return JX_OK;
+    auto enc = tensor_map_encoder();
+    if (!enc) return fail(JX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if (kv->esz != 2) return fail(JX_ERR_UNSUPPORTED, "tensor-core prefill needs a 16-bit cache");
+    const cuuint64_t dims[4] = {kv->d.row_stride, kv->d.capacity, kv->d.n_layers, kv->d.n_seqs};
+    const cuuint64_t strides[3] = {
+        static_cast<cuuint64_t>(kv->d.row_stride) * 2,
+        static_cast<cuuint64_t>(kv->d.row_stride) * 2 * kv->d.capacity,
+        static_cast<cuuint64_t>(kv->d.row_stride) * 2 * kv->d.capacity * kv->d.n_layers};
+    const cuuint32_t box[4] = {64, static_cast<cuuint32_t>(rows), 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    for (int which = 0; which < 2; ++which) {
+        CUresult r = enc(which == 0 ? &kv->tmKp[kind] : &kv->tmVp[kind],
+                         CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, which == 0 ? kv->k : kv->v, dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(JX_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    }
+    kv->tmp_ok[kind] = true;
     return JX_OK;
 }
 
@@ -552,6 +584,193 @@ int check_step_ptr(const void* p, const char* name, int device, bool* host) {
                 "or another device's memory would fault the kernel)", name, device);
 }
 
+// Plan and launch of the tensor-core prefill for one launch group (layers of
+// one head_dim; their rows were appended already).  Rows of the call that
+// belong to one sequence at consecutive positions (in call order) form runs;
+// each run is cut into tiles of 128/G tokens, and a work item is (tile, layer,
+// kv head).  Items go largest first (streamed K/V tiles) so the persistent
+// CTAs, which take items c, c + P, ..., finish close together.  Each tile has
+// its own run of (cos, sin) rows, computed with apply_rope's expressions.
+int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
+               const std::vector<uint32_t>& grp_layers, const jx_step_args* a,
+               const std::vector<int>& seqs, int hd, uint32_t G, bool neox, float inv_cap,
+               size_t gi, cudaStream_t stream) {
+    const jx_kv_desc& D = kv->d;
+    const int TQ = 128 / static_cast<int>(G);
+    const int BN = prefill_tc_rows(hd);
+    const int kind = hd == 64 ? 0 : 1;
+    int rc = encode_prefill_maps(kv, kind, BN);
+    if (rc) return rc;
+    std::vector<std::pair<uint32_t, uint32_t>> chunks;  // (first row, tokens)
+    for (uint32_t r = 0; r < a->n_seqs;) {
+        uint32_t nb = 1;
+        while (nb < static_cast<uint32_t>(TQ) && r + nb < a->n_seqs && seqs[r + nb] == seqs[r] &&
+               a->pos[r + nb] == a->pos[r] + static_cast<int32_t>(nb))
+            ++nb;
+        chunks.emplace_back(r, nb);
+        r += nb;
+    }
+    const int width = hd / 2;
+    std::vector<PrefillTile> items;
+    items.reserve(chunks.size() * grp_layers.size() * a->n_kv_heads);
+    std::vector<PairRow> appends;  // append pass: one row per (chunk, layer)
+    appends.reserve(chunks.size() * grp_layers.size());
+    std::vector<float2> rope;
+    std::map<std::tuple<uint32_t, uint32_t, uint32_t, uint64_t, uint32_t, uint32_t>, int> rope_ids;
+    std::map<std::tuple<uint32_t, uint32_t, uint64_t>, std::vector<float>> inv_freqs;
+    int n_rope = 0;
+    const uint32_t W = a->sliding_window;
+    for (const auto& ch : chunks) {
+        const uint32_t r0 = ch.first, nt = ch.second;
+        const uint32_t pos0 = static_cast<uint32_t>(a->pos[r0]);
+        for (uint32_t l : grp_layers) {
+            const jx_layer_desc& L = layers[l];
+            // every row the chunk attends must be in this cache (as for a step)
+            const uint64_t t0 = (L.is_swa && W > 0 && pos0 >= W) ? pos0 - W + 1 : 0;
+            const uint64_t last = static_cast<uint64_t>(pos0) + nt - 1;
+            if (t0 < D.pos_base || last >= static_cast<uint64_t>(D.pos_base) + D.capacity)
+                return fail(JX_ERR_RANGE,
+                            "position %llu (window start %llu) is outside the cache rows "
+                            "[%u, %llu); compact or roll back first",
+                            static_cast<unsigned long long>(last),
+                            static_cast<unsigned long long>(t0), D.pos_base,
+                            static_cast<unsigned long long>(D.pos_base) + D.capacity);
+            const uint32_t rdim = std::min(L.head_dim, L.rope_dim);
+            const float* rf = (neox && !L.is_swa && L.rope_freqs) ? L.rope_freqs : nullptr;
+            uint32_t base_bits, yarn_bits;
+            std::memcpy(&base_bits, &L.rope_freq_base, 4);
+            std::memcpy(&yarn_bits, &a->yarn_scale, 4);
+            const uint64_t fh = rf ? hash_floats(rf, rdim / 2) : 0;
+            const auto key = std::make_tuple(rdim, base_bits, yarn_bits, fh, pos0, nt);
+            auto itk = rope_ids.find(key);
+            int rid;
+            if (itk == rope_ids.end()) {
+                rid = n_rope;
+                rope_ids.emplace(key, rid);
+                n_rope += static_cast<int>(nt);
+                rope.resize(static_cast<size_t>(n_rope) * width);
+                const auto fkey = std::make_tuple(rdim, base_bits, fh);
+                auto itf = inv_freqs.find(fkey);
+                if (itf == inv_freqs.end()) {
+                    std::vector<float> f(rdim / 2);
+                    rope_inv_freqs(L.head_dim, L.rope_dim, L.rope_freq_base, neox, rf, f.data());
+                    itf = inv_freqs.emplace(fkey, std::move(f)).first;
+                }
+                for (uint32_t j = 0; j < nt; ++j)
+                    rope_row_freqs(itf->second.data(), rdim / 2, pos0 + j, a->yarn_scale,
+                                   rope.data() + static_cast<size_t>(rid + j) * width, width);
+            } else {
+                rid = itk->second;
+            }
+            PrefillTile t{};
+            t.seq = seqs[r0];
+            t.cache_layer = static_cast<int>(L.kv_source_layer);
+            t.io0 = static_cast<int>(r0 * n_layers + l);
+            t.io_step = static_cast<int>(n_layers);
+            t.tok_row0 = static_cast<int>(pos0) - static_cast<int>(D.pos_base);
+            t.ntok = static_cast<int>(nt);
+            t.row0 = 0;  // local row 0: non-window layers need pos_base == 0 (checked above)
+            t.window = (L.is_swa && W > 0) ? static_cast<int>(W) : 0;
+            t.rope_row0 = rid;
+            t.rope_half = static_cast<int>(rdim / 2);
+            t.kv_lo = t.window > 0 ? std::max(0, t.tok_row0 - t.window + 1) : 0;
+            t.n_tiles = (t.tok_row0 + t.ntok - t.kv_lo + BN - 1) / BN;
+            for (uint32_t h = 0; h < a->n_kv_heads; ++h) {
+                t.kvh = static_cast<int>(h);
+                items.push_back(t);
+            }
+            // the chunk's rows of this layer, appended before any is attended
+            // (one block per chunk and layer; shares-KV layers append nothing)
+            PairRow ap{};
+            ap.seq = t.seq;
+            ap.io = t.io0;
+            ap.io_step = t.io_step;
+            ap.nq = t.ntok;
+            ap.cache_layer = t.cache_layer;
+            ap.append_row = L.shares_kv ? -1 : t.tok_row0;
+            ap.rope_row = rid;
+            ap.rope_half = t.rope_half;
+            appends.push_back(ap);
+        }
+    }
+    // The kernel trusts the plan: validate every item here.
+    for (const PrefillTile& t : items) {
+        const bool ok =
+            t.seq >= 0 && t.seq < static_cast<int>(D.n_seqs) && t.cache_layer >= 0 &&
+            t.cache_layer < static_cast<int>(D.n_layers) && t.kvh >= 0 &&
+            static_cast<uint64_t>(t.kvh + 1) * hd <= D.row_stride && t.ntok >= 1 && t.ntok <= TQ &&
+            t.tok_row0 >= 0 && static_cast<uint64_t>(t.tok_row0) + t.ntok <= D.capacity &&
+            t.kv_lo >= 0 && t.kv_lo <= t.tok_row0 && t.n_tiles >= 1 && t.io0 >= 0 &&
+            static_cast<long long>(t.io0) + static_cast<long long>(t.ntok - 1) * t.io_step <
+                static_cast<long long>(a->n_seqs) * n_layers &&
+            t.rope_row0 >= 0 && t.rope_row0 + t.ntok <= n_rope && t.rope_half >= 0 &&
+            t.rope_half <= hd / 2;
+        if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent prefill work item");
+    }
+    std::stable_sort(items.begin(), items.end(), [](const PrefillTile& x, const PrefillTile& y) {
+        return x.n_tiles > y.n_tiles;
+    });
+    for (const PairRow& ap : appends) {
+        const bool ok = ap.append_row < 0 ||
+                        (ap.append_row >= 0 &&
+                         static_cast<uint64_t>(ap.append_row) + ap.nq <= D.capacity &&
+                         ap.rope_row + ap.nq <= n_rope &&
+                         static_cast<uint64_t>(a->n_kv_heads) * hd <= D.row_stride &&
+                         static_cast<uint64_t>(a->n_kv_heads) * hd <= a->kv_stride);
+        if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent prefill append row");
+    }
+    const size_t item_bytes = items.size() * sizeof(PrefillTile);
+    const size_t app_off = (item_bytes + 255) & ~static_cast<size_t>(255);
+    const size_t app_bytes = appends.size() * sizeof(PairRow);
+    const size_t rope_off = (app_off + app_bytes + 255) & ~static_cast<size_t>(255);
+    std::vector<unsigned char> bytes(rope_off + rope.size() * sizeof(float2), 0);
+    std::memcpy(bytes.data(), items.data(), item_bytes);
+    std::memcpy(bytes.data() + app_off, appends.data(), app_bytes);
+    if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope.size() * sizeof(float2));
+    const size_t slot = gi;
+    rc = upload_plan(kv, slot, bytes, stream);
+    if (rc) return rc;
+    {
+        unsigned char* dplan = static_cast<unsigned char*>(kv->slots[slot].d_buf);
+        const PairRow* dp = reinterpret_cast<const PairRow*>(dplan + app_off);
+        const float2* dr = reinterpret_cast<const float2*>(dplan + rope_off);
+        const int np = static_cast<int>(appends.size());
+        const int nkv = static_cast<int>(a->n_kv_heads);
+        if (D.dtype == JX_BF16)
+            append_rows_kernel<DT_BF16><<<np, 256, 0, stream>>>(
+                dp, np, dr, width, a->k, a->v, a->kv_stride, nkv, hd, neox ? 1 : 0, kv->k, kv->v,
+                kv->seq_stride, kv->layer_stride, D.row_stride);
+        else
+            append_rows_kernel<DT_F16T><<<np, 256, 0, stream>>>(
+                dp, np, dr, width, a->k, a->v, a->kv_stride, nkv, hd, neox ? 1 : 0, kv->k, kv->v,
+                kv->seq_stride, kv->layer_stride, D.row_stride);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess)
+            return fail(JX_ERR_CUDA, "append launch failed: %s", cudaGetErrorString(e));
+    }
+    PrefillArgs pa{};
+    pa.tiles = static_cast<const PrefillTile*>(kv->slots[slot].d_buf);
+    pa.n_items = static_cast<int>(items.size());
+    pa.neox = neox ? 1 : 0;
+    pa.q = a->q;
+    pa.out = a->out;
+    pa.q_stride = a->q_stride;
+    pa.rope = reinterpret_cast<const float2*>(static_cast<unsigned char*>(kv->slots[slot].d_buf) +
+                                              rope_off);
+    pa.scale = a->scale;
+    pa.softcap = a->softcap;
+    pa.inv_softcap = inv_cap;
+    pa.err = kv->d_err;
+    pa.dbg = kv->d_dbg;
+    pa.wait_limit = wait_limit_cycles(kv->opt_wait_limit_ms);
+    const int grid = static_cast<int>(std::min<size_t>(std::max(kv->num_sms, 1), items.size()));
+    const cudaError_t e = prefill_tc_launch(pa, &kv->tmKp[kind], &kv->tmVp[kind], hd, D.dtype,
+                                            static_cast<int>(G), grid, stream);
+    if (e != cudaSuccess)
+        return fail(JX_ERR_CUDA, "tensor-core prefill launch failed: %s", cudaGetErrorString(e));
+    return JX_OK;
+}
+
 int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const jx_step_args* a,
               float* partials, cudaStream_t stream, bool prefill = false) {
     if (!kv || !layers || !a) return fail(JX_ERR_INVALID, "null handle, layers or args");
@@ -671,6 +890,16 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     for (size_t gi = 0; gi < groups.size(); ++gi) {
         const Group& grp = groups[gi];
         const int hd = grp.hd;
+        if (prefill && kv->opt_prefill_tc && gp == static_cast<int>(G) &&
+            prefill_tc_supported(hd, D.dtype, static_cast<int>(G))) {
+            // 16-bit cache: append pass, then the prompt's attention on the
+            // tensor cores, every K/V tile shared by 128/G tokens x G heads
+            const int rc = prefill_tc(kv, layers, n_layers, grp.layers, a, seqs, hd, G, neox,
+                                      inv_cap, gi, stream);
+            if (rc) return rc;
+            ++launches;
+            continue;
+        }
         // Prefill blocks: up to 8/G consecutive tokens of a sequence share one
         // pair (8 query columns: token x head), so their rows stream once.
         const int nq_max =
@@ -1507,6 +1736,7 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
     else if (!std::strcmp(key, "split_penalty_us"))
         kv->opt_split_penalty_us = value < 0 ? -1.0f : static_cast<float>(value);
     else if (!std::strcmp(key, "wait_limit_ms")) kv->opt_wait_limit_ms = value;
+    else if (!std::strcmp(key, "prefill_tc")) kv->opt_prefill_tc = value ? 1 : 0;
     else if (!std::strcmp(key, "test_wait_cta")) kv->opt_test_wait_cta = value;
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;

@@ -1,0 +1,528 @@
+// jx_prefill_tc.cu -- causal prompt attention on the 5th-generation tensor
+// cores (tcgen05, TMEM accumulators) for 16-bit KV caches.
+//
+// jxai feeds a prompt token by token through forward_token
+// (src/transformer.cpp:3092-3095): token j appends its row and attends over
+// every earlier row of its sequence (sliding-window layers: the last W rows,
+// :2524-2527), with the block of :2530-2566.  jx_attn_prefill appends every
+// row first (append_rows_kernel); this kernel then computes all tokens'
+// attention at once, sharing every K/V tile across a tile of query rows:
+//
+//  * Work item = (run of consecutive prompt tokens of one sequence, layer,
+//    kv head): TQ = 128/G tokens x the G query heads of that kv head are the
+//    M = 128 rows of the MMAs (row r = token r/G, head r%G).
+//  * Warp 0 streams K and V tiles of BN cache rows (BN = 128 at head_dim 64,
+//    64 at head_dim 128) into a 3-stage ring with TMA (128-byte swizzle, no
+//    multicast).  Warp 1 owns the tensor memory (512 columns) and issues the
+//    MMAs from one thread: S = Q.K^T into one of two TMEM buffers, then
+//    O_t = P.V into one of two others.  Warps 2-5 (one thread per query row =
+//    TMEM lane) rotate and stage Q, read S with tcgen05.ld, apply the scale,
+//    soft-cap and each row's causal / window limits, run the online softmax,
+//    stage P, and fold each tile's O_t into registers with the rescale.
+//  * Precision.  q and p are fp32; each is split into two 16-bit parts
+//    (hi = rn(x), lo = rn(x - hi)) and both parts are multiplied into the same
+//    fp32 accumulator, while cache values are exact in the operand type -- the
+//    fp32-level result the 1e-4 bar needs (a numpy model of this arithmetic
+//    stays within 1.3e-6 of float64 attention; one 16-bit part is 2-7e-4).
+//    fp16 q rows are scaled by a power of two into [2^14, 2^15) first and the
+//    scale is taken off S exactly.
+//  * Unattended V rows past the prompt's last row in the last tile are
+//    cleared in shared memory before P.V (0 * Inf would otherwise leak).
+//  * Every mbarrier wait is bounded; a wait that runs out raises the CTA's
+//    abort flag and the device error word, and every role finishes its
+//    control flow, waits for its copies / MMAs in flight and frees TMEM.
+#include "jx_device.cuh"
+#include "jx_internal.h"
+
+namespace jx {
+namespace {
+
+constexpr float kLog2eP = 1.4426950408889634f;
+
+// Loads 32 consecutive 32-bit TMEM columns of this thread's lane and waits
+// for them (one asm statement: the registers are valid when it ends).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Loads 64 consecutive 32-bit TMEM columns of this thread's lane and waits
+// for them (one asm statement: the registers are valid when it ends).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Loads 128 consecutive 32-bit TMEM columns of this thread's lane and waits
+// for them (one asm statement: the registers are valid when it ends).
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&r)[128]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, %80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, %96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, %112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]), "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]), "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]), "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]), "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]), "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]), "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]), "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]), "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+// Orders tcgen05 operations before / after a thread synchronisation (an
+// mbarrier arrive / wait or a CTA barrier).
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// The mbarrier completes once every tcgen05 operation this thread issued
+// before has completed.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T, one CTA, 16-bit operands, fp32 accumulator.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor of a 128-byte-swizzled operand tile (the
+// layout TMA's SWIZZLE_128B writes: 128-byte rows, 16-byte chunk c of row r at
+// chunk c ^ (r % 8), tile base 1024-byte aligned).  lbo / sbo in bytes:
+// K-major operands: lbo unused (16), sbo = 1024 (8 rows of 128 bytes);
+// MN-major operands: lbo = distance between 64-element column blocks, sbo =
+// 1024 (8 K-rows).  Bits 46-47 = 1 (tcgen05 descriptor), 61-63 = 2 (128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) |
+           (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+           (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulation: A and B both
+// bf16 (DT_BF16) or both fp16, A K-major, B K-major or MN-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int dt, int M, int N, bool b_mn) {
+    return (1u << 4) | ((dt == DT_BF16 ? 1u : 0u) << 7) | ((dt == DT_BF16 ? 1u : 0u) << 10) |
+           ((b_mn ? 1u : 0u) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+           (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+template <int HD>
+struct PfCfg {
+    static constexpr int BN = HD == 64 ? 128 : 64;  // cache rows per K/V tile
+    static constexpr int NS = 3;                    // K/V ring stages
+    static constexpr int NSLAB = HD / 64;           // 128-byte slabs of a head row
+    static constexpr int KSLAB = BN * 128;          // one slab of a K or V tile
+    static constexpr int TILE_B = KSLAB * NSLAB;    // K (or V) tile
+    static constexpr int STAGE_B = 2 * TILE_B;
+    static constexpr int QSLAB = 128 * 128;         // 128 rows x 64 elements
+    static constexpr int QPART = QSLAB * NSLAB;     // one 16-bit part of Q
+    static constexpr int PSLAB = 128 * 128;
+    static constexpr int PNSLAB = BN / 64;
+    static constexpr int PPART = PSLAB * PNSLAB;    // one 16-bit part of P
+    static constexpr int OFF_Q = NS * STAGE_B;
+    static constexpr int OFF_P = OFF_Q + 2 * QPART;
+    static constexpr int OFF_BAR = OFF_P + 2 * PPART;
+    // barriers: kv_full[NS], kv_empty[NS], q_full, q_empty, s_full[2],
+    // s_empty[2], p_full, p_empty, o_full[2], o_empty[2], done
+    static constexpr int B_KVF = 0, B_KVE = NS, B_QF = 2 * NS, B_QE = B_QF + 1, B_SF = B_QF + 2,
+                         B_SE = B_SF + 2, B_PF = B_SE + 2, B_PE = B_PF + 1, B_OF = B_PE + 1,
+                         B_OE = B_OF + 2, B_DONE = B_OE + 2, NBARS = B_DONE + 1;
+    static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // TMEM base, abort flag
+    static constexpr int SMEM = OFF_MISC + 16 + 1024;     // + alignment slack
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int COL_S = 0;        // S buffers: columns [0, 2 BN)
+    static constexpr int COL_O = 2 * BN;   // O tile buffers: [2 BN, 2 BN + 2 HD)
+    static_assert(COL_O + 2 * HD <= TMEM_COLS, "TMEM budget");
+    static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+template <int HD, int DT, int G>
+__global__ void __launch_bounds__(192, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                      const PrefillArgs a) {
+    using C = PfCfg<HD>;
+    constexpr int BN = C::BN;
+    static_assert(128 % G == 0 && G <= 8, "query group");
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    unsigned char* base = smem_raw + (sbase - raw);
+    const uint32_t bars = sbase + C::OFF_BAR;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::OFF_MISC);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::OFF_MISC + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long wlim = a.wait_limit > 0 ? a.wait_limit : kWaitLimitCycles;
+    const int P = gridDim.x;
+#define BAR(i) (bars + 8u * static_cast<uint32_t>(i))
+#define WAIT(i, par, site, idx) \
+    mbar_wait_bounded(BAR(i), (par), abort_flag, a.err, a.dbg, (site), (idx), true, wlim)
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::NS; ++s) {
+            mbar_init(BAR(C::B_KVF + s), 1);
+            mbar_init(BAR(C::B_KVE + s), 1);
+        }
+        mbar_init(BAR(C::B_QF), 4);
+        mbar_init(BAR(C::B_QE), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(BAR(C::B_SF + s), 1);
+            mbar_init(BAR(C::B_SE + s), 4);
+            mbar_init(BAR(C::B_OF + s), 1);
+            mbar_init(BAR(C::B_OE + s), 4);
+        }
+        mbar_init(BAR(C::B_PF), 4);
+        mbar_init(BAR(C::B_PE), 1);
+        mbar_init(BAR(C::B_DONE), 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tensormap(&tmK);
+            prefetch_tensormap(&tmV);
+        }
+        int g = 0, n_issued = 0;
+        for (int it = blockIdx.x; it < a.n_items; it += P) {
+            const PrefillTile tl = a.tiles[it];
+            for (int t = 0; t < tl.n_tiles; ++t, ++g) {
+                const int st = g % C::NS;
+                if (g >= C::NS) WAIT(C::B_KVE + st, ((g / C::NS) & 1) ^ 1u, 21, g);
+                const bool issue = __shfl_sync(0xffffffffu, *abort_flag == 0 ? 1 : 0, 0) != 0;
+                if (!issue) continue;
+                n_issued = g + 1;
+                if (lane == 0) {
+                    const uint32_t fb = BAR(C::B_KVF + st);
+                    mbar_arrive_expect_tx(fb, C::STAGE_B);
+                    const uint32_t dk = sbase + st * C::STAGE_B, dv = dk + C::TILE_B;
+                    const int row = tl.kv_lo + t * BN;
+#pragma unroll
+                    for (int b = 0; b < C::NSLAB; ++b) {
+                        const int x = tl.kvh * HD + b * 64;
+                        tma_load_4d(dk + b * C::KSLAB, &tmK, fb, x, row, tl.cache_layer, tl.seq);
+                        tma_load_4d(dv + b * C::KSLAB, &tmV, fb, x, row, tl.cache_layer, tl.seq);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        // every issued tile lands before the CTA exits
+        for (int k = n_issued > C::NS ? n_issued - C::NS : 0; k < n_issued; ++k)
+            mbar_wait_bounded(BAR(C::B_KVF + k % C::NS), (k / C::NS) & 1, abort_flag, a.err, a.dbg,
+                              23, k, false, kDrainLimitCycles);
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        constexpr uint32_t ID_S = idesc_f16(DT, 128, BN, false);
+        constexpr uint32_t ID_PV = idesc_f16(DT, 128, HD, true);
+        int g = 0, itc = 0;
+        for (int it = blockIdx.x; it < a.n_items; it += P, ++itc) {
+            const PrefillTile tl = a.tiles[it];
+            const int n = tl.n_tiles;
+            WAIT(C::B_QF, itc & 1, 24, itc);  // Q of this item staged
+            tc_fence_after();
+            // S = Q_hi.K^T + Q_lo.K^T for global tile gg
+            auto issue_s = [&](int gg) {
+                const int st = gg % C::NS;
+                WAIT(C::B_KVF + st, (gg / C::NS) & 1, 25, gg);
+                const int sb = gg & 1;
+                if (gg >= 2) WAIT(C::B_SE + sb, ((gg >> 1) - 1) & 1, 26, gg);
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t d = tmem + C::COL_S + sb * BN;
+                    const uint32_t kb = sbase + st * C::STAGE_B;
+#pragma unroll
+                    for (int part = 0; part < 2; ++part)
+#pragma unroll
+                        for (int ks = 0; ks < HD / 16; ++ks) {
+                            const uint64_t ad = sw128_desc(sbase + C::OFF_Q + part * C::QPART +
+                                                               (ks / 4) * C::QSLAB + (ks % 4) * 32,
+                                                           16, 1024);
+                            const uint64_t bd =
+                                sw128_desc(kb + (ks / 4) * C::KSLAB + (ks % 4) * 32, 16, 1024);
+                            tc_mma(d, ad, bd, ID_S, (part | ks) != 0 ? 1u : 0u);
+                        }
+                    tc_commit(BAR(C::B_SF + sb));
+                }
+                __syncwarp();
+            };
+            if (n > 0) issue_s(g);
+            for (int t = 0; t < n; ++t, ++g) {
+                if (t + 1 < n) issue_s(g + 1);
+                WAIT(C::B_PF, g & 1, 27, g);  // P(g) staged
+                const int ob = g & 1;
+                if (g >= 2) WAIT(C::B_OE + ob, ((g >> 1) - 1) & 1, 28, g);
+                tc_fence_after();
+                const int st = g % C::NS;
+                const uint32_t vb = sbase + st * C::STAGE_B + C::TILE_B;
+                if (t == n - 1) {
+                    // rows past the prompt's last row: V := 0 (p is 0 there)
+                    const int z0 = tl.tok_row0 + tl.ntok - (tl.kv_lo + t * BN);
+                    if (z0 < BN) {
+                        unsigned char* vt = base + st * C::STAGE_B + C::TILE_B;
+                        for (int b = 0; b < C::NSLAB; ++b)
+                            for (int idx = lane; idx < (BN - z0) * 8; idx += 32)
+                                *reinterpret_cast<uint4*>(vt + b * C::KSLAB + (z0 + idx / 8) * 128 +
+                                                          (idx % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
+                        fence_proxy_async_shared();
+                    }
+                    __syncwarp();
+                }
+                if (lane == 0) {
+                    const uint32_t d = tmem + C::COL_O + ob * HD;
+#pragma unroll
+                    for (int part = 0; part < 2; ++part)
+#pragma unroll
+                        for (int kb = 0; kb < BN / 16; ++kb) {
+                            const uint64_t ad = sw128_desc(sbase + C::OFF_P + part * C::PPART +
+                                                               (kb / 4) * C::PSLAB + (kb % 4) * 32,
+                                                           16, 1024);
+                            const uint64_t bd = sw128_desc(vb + kb * 16 * 128, C::KSLAB, 1024);
+                            tc_mma(d, ad, bd, ID_PV, (part | kb) != 0 ? 1u : 0u);
+                        }
+                    tc_commit(BAR(C::B_OF + ob));
+                    tc_commit(BAR(C::B_PE));
+                    tc_commit(BAR(C::B_KVE + st));
+                }
+                __syncwarp();
+            }
+            if (lane == 0) tc_commit(BAR(C::B_QE));  // this item's Q is no longer read
+            __syncwarp();
+        }
+        // every MMA this thread issued completes before TMEM is freed
+        if (lane == 0) tc_commit(BAR(C::B_DONE));
+        __syncwarp();
+        mbar_wait_bounded(BAR(C::B_DONE), 0u, abort_flag, a.err, a.dbg, 29, 0, false,
+                          kDrainLimitCycles);
+    } else {
+        // ------------------------------------------------------------ softmax warps
+        const int q4 = warp & 3;           // this warp's TMEM lane quarter
+        const int r = q4 * 32 + lane;      // query row of the tile = TMEM lane
+        const int j = r / G, h = r % G;    // token of the tile, head within the kv group
+        const uint32_t lane_addr = static_cast<uint32_t>(q4 * 32) << 16;
+        int g = 0, itc = 0;
+        for (int it = blockIdx.x; it < a.n_items; it += P, ++itc) {
+            const PrefillTile tl = a.tiles[it];
+            const bool live = j < tl.ntok;
+            const int hi_r = live ? tl.tok_row0 + j : -1;
+            const int lo_r = live ? (tl.window > 0 ? max(tl.row0, hi_r - tl.window + 1) : tl.row0) : 0;
+            const long long io = static_cast<long long>(tl.io0) + static_cast<long long>(j) * tl.io_step;
+            // ---- Q: rotate, split into hi / lo, stage (swizzled, K-major)
+            if (itc > 0) WAIT(C::B_QE, (itc - 1) & 1, 30, itc);
+            float unscale = 1.0f;
+            {
+                float qr[HD];
+                float mx = 0.0f;
+                const float* qin = a.q + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD;
+                const float2* cs = a.rope + static_cast<long long>(tl.rope_row0 + j) * (HD / 2);
+#pragma unroll
+                for (int d = 0; d < HD; ++d) {
+                    qr[d] = live ? rope_elem(qin, d, tl.rope_half, cs, a.neox != 0) : 0.0f;
+                    mx = fmaxf(mx, fabsf(qr[d]));
+                }
+                float up = 1.0f;
+                if constexpr (DT == DT_F16T) {
+                    const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu) - 127;
+                    const int sh = min(60, max(-60, 14 - e));
+                    up = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
+                    unscale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+                }
+#pragma unroll
+                for (int c = 0; c < HD / 8; ++c) {
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        split_pair<DT>(qr[8 * c + 2 * i] * up, qr[8 * c + 2 * i + 1] * up, hw[i], lw[i]);
+                    const int off = C::OFF_Q + (c / 8) * C::QSLAB + r * 128 + (((c % 8) ^ (r & 7)) * 16);
+                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(base + off + C::QPART) =
+                        make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+            }
+            fence_proxy_async_shared();  // generic writes -> tensor-core reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(BAR(C::B_QF));
+
+            float m = -INFINITY, l = 0.0f, alpha_pend = 0.0f;
+            float o[HD];
+#pragma unroll
+            for (int d = 0; d < HD; ++d) o[d] = 0.0f;
+            // folds tile gg's O (relative to its running max) into o
+            auto add_o = [&](int gg, float alpha) {
+                const int ob = gg & 1;
+                WAIT(C::B_OF + ob, (gg >> 1) & 1, 31, gg);
+                __syncwarp();  // converged for the .sync.aligned loads
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    uint32_t t32[32];
+                    tmem_ld32(tmem + lane_addr + C::COL_O + ob * HD + c, t32);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, __uint_as_float(t32[i]));
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(BAR(C::B_OE + ob));
+            };
+            const int n = tl.n_tiles;
+            for (int t = 0; t < n; ++t, ++g) {
+                const int sb = g & 1;
+                WAIT(C::B_SF + sb, (g >> 1) & 1, 32, g);
+                __syncwarp();  // converged for the .sync.aligned load
+                tc_fence_after();
+                uint32_t sr[BN];
+                if constexpr (BN == 128) tmem_ld128(tmem + lane_addr + C::COL_S + sb * BN, sr);
+                else tmem_ld64(tmem + lane_addr + C::COL_S + sb * BN, sr);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(BAR(C::B_SE + sb));
+                // scores of this row: scale, soft-cap, causal / window limits
+                const int c0 = tl.kv_lo + t * BN;
+                float mt = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < BN; ++c) {
+                    float v = __fmul_rn(__uint_as_float(sr[c]) * unscale, a.scale);
+                    if (a.softcap > 0.0f) v = __fmul_rn(a.softcap, tanhf(__fmul_rn(v, a.inv_softcap)));
+                    const int col = c0 + c;
+                    v = (col >= lo_r && col <= hi_r) ? v : -INFINITY;
+                    sr[c] = __float_as_uint(v);
+                    mt = fmaxf(mt, v);
+                }
+                const float mn = fmaxf(m, mt);
+                const float alpha = m == -INFINITY ? 0.0f : ex2_approx((m - mn) * kLog2eP);
+                m = mn;
+                // P(g) -> shared memory once P.V of the previous tile has read it
+                if (g >= 1) WAIT(C::B_PE, (g - 1) & 1, 33, g);
+                float ls = 0.0f;
+#pragma unroll
+                for (int c8 = 0; c8 < BN / 8; ++c8) {
+                    float pv[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float s = __uint_as_float(sr[8 * c8 + i]);
+                        pv[i] = s == -INFINITY ? 0.0f : ex2_approx((s - mn) * kLog2eP);
+                        ls += pv[i];
+                    }
+                    uint32_t hw[4], lw[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) split_pair<DT>(pv[2 * i], pv[2 * i + 1], hw[i], lw[i]);
+                    const int off =
+                        C::OFF_P + (c8 / 8) * C::PSLAB + r * 128 + (((c8 % 8) ^ (r & 7)) * 16);
+                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(base + off + C::PPART) =
+                        make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                }
+                fence_proxy_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(BAR(C::B_PF));
+                l = l * alpha + ls;
+                if (t >= 1) add_o(g - 1, alpha_pend);
+                alpha_pend = alpha;
+            }
+            if (n > 0) add_o(g - 1, alpha_pend);
+            // ---- output row: o / l
+            if (live && l > 0.0f) {
+                const float inv = 1.0f / l;
+                float* dst = a.out + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD;
+#pragma unroll
+                for (int d = 0; d < HD; d += 4)
+                    *reinterpret_cast<float4*>(dst + d) =
+                        make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+            }
+        }
+    }
+#undef WAIT
+#undef BAR
+    // every role is done with TMEM: tcgen05.ld completed (wait::ld), MMAs
+    // observed through the done barrier
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+template <int HD, int DT, int G>
+cudaError_t launch_one(const PrefillArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, int grid,
+                       cudaStream_t st) {
+    constexpr int smem = PfCfg<HD>::SMEM;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        const cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<HD, DT, G>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    prefill_tc_kernel<HD, DT, G><<<grid, 192, smem, st>>>(*tk, *tv, a);
+    return cudaGetLastError();
+}
+
+template <int HD, int DT>
+cudaError_t launch_g(const PrefillArgs& a, const CUtensorMap* tk, const CUtensorMap* tv, int G,
+                     int grid, cudaStream_t st) {
+    switch (G) {
+        case 1: return launch_one<HD, DT, 1>(a, tk, tv, grid, st);
+        case 2: return launch_one<HD, DT, 2>(a, tk, tv, grid, st);
+        case 4: return launch_one<HD, DT, 4>(a, tk, tv, grid, st);
+        case 8: return launch_one<HD, DT, 8>(a, tk, tv, grid, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+bool prefill_tc_supported(int head_dim, int dtype, int G) {
+    return (head_dim == 64 || head_dim == 128) && (dtype == DT_BF16 || dtype == DT_F16T) &&
+           (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+int prefill_tc_rows(int head_dim) { return head_dim == 64 ? PfCfg<64>::BN : PfCfg<128>::BN; }
+
+cudaError_t prefill_tc_launch(const PrefillArgs& a, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                              int head_dim, int dtype, int G, int grid, cudaStream_t stream) {
+    if (!prefill_tc_supported(head_dim, dtype, G)) return cudaErrorInvalidValue;
+    if (head_dim == 64)
+        return dtype == DT_BF16 ? launch_g<64, DT_BF16>(a, tmK, tmV, G, grid, stream)
+                                : launch_g<64, DT_F16T>(a, tmK, tmV, G, grid, stream);
+    return dtype == DT_BF16 ? launch_g<128, DT_BF16>(a, tmK, tmV, G, grid, stream)
+                            : launch_g<128, DT_F16T>(a, tmK, tmV, G, grid, stream);
+}
+
+}  // namespace jx
