@@ -15,10 +15,12 @@
 //    64 at head_dim 128) into a 3-stage ring with TMA (128-byte swizzle, no
 //    multicast).  Warp 1 owns the tensor memory (512 columns) and issues the
 //    MMAs from one thread: S = Q.K^T into one of two TMEM buffers, then
-//    O_t = P.V into one of two others.  Warps 2-5 (one thread per query row =
-//    TMEM lane) rotate and stage Q, read S with tcgen05.ld, apply the scale,
-//    soft-cap and each row's causal / window limits, run the online softmax,
-//    stage P, and fold each tile's O_t into registers with the rescale.
+//    O_t = P.V into one of two others.  Warps 2-9 (two per TMEM lane quarter,
+//    each with half of a row's columns; one thread per query row = TMEM lane)
+//    rotate and stage Q, read S with tcgen05.ld, apply the scale, soft-cap
+//    and each row's causal / window limits, run the online softmax (row
+//    maxima exchanged between the two halves), stage P, and fold each tile's
+//    O_t into registers with the rescale.
 //  * Precision.  q and p are fp32; each is split into two 16-bit parts
 //    (hi = rn(x), lo = rn(x - hi)) and both parts are multiplied into the same
 //    fp32 accumulator, while cache values are exact in the operand type -- the
@@ -38,6 +40,8 @@ namespace jx {
 namespace {
 
 constexpr float kLog2eP = 1.4426950408889634f;
+constexpr int kSoftmaxWarps = 8;                       // warps 2-9
+constexpr int kPfThreads = 32 * (2 + kSoftmaxWarps);   // + TMA warp, MMA warp
 
 // Loads 32 consecutive 32-bit TMEM columns of this thread's lane and waits
 // for them (one asm statement: the registers are valid when it ends).
@@ -153,7 +157,8 @@ struct PfCfg {
                          B_SE = B_SF + 2, B_PF = B_SE + 2, B_PE = B_PF + 1, B_OF = B_PE + 1,
                          B_OE = B_OF + 2, B_DONE = B_OE + 2, NBARS = B_DONE + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // TMEM base, abort flag
-    static constexpr int SMEM = OFF_MISC + 16 + 1024;     // + alignment slack
+    static constexpr int OFF_XCH = OFF_MISC + 16;         // [2][2][128] floats: row exchanges
+    static constexpr int SMEM = OFF_XCH + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
     static constexpr int TMEM_COLS = 512;
     static constexpr int COL_S = 0;        // S buffers: columns [0, 2 BN)
     static constexpr int COL_O = 2 * BN;   // O tile buffers: [2 BN, 2 BN + 2 HD)
@@ -162,7 +167,7 @@ struct PfCfg {
 };
 
 template <int HD, int DT, int G>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kPfThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                       const PrefillArgs a) {
     using C = PfCfg<HD>;
@@ -187,15 +192,15 @@ __global__ void __launch_bounds__(192, 1)
             mbar_init(BAR(C::B_KVF + s), 1);
             mbar_init(BAR(C::B_KVE + s), 1);
         }
-        mbar_init(BAR(C::B_QF), 4);
+        mbar_init(BAR(C::B_QF), kSoftmaxWarps);
         mbar_init(BAR(C::B_QE), 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(BAR(C::B_SF + s), 1);
-            mbar_init(BAR(C::B_SE + s), 4);
+            mbar_init(BAR(C::B_SE + s), kSoftmaxWarps);
             mbar_init(BAR(C::B_OF + s), 1);
-            mbar_init(BAR(C::B_OE + s), 4);
+            mbar_init(BAR(C::B_OE + s), kSoftmaxWarps);
         }
-        mbar_init(BAR(C::B_PF), 4);
+        mbar_init(BAR(C::B_PF), kSoftmaxWarps);
         mbar_init(BAR(C::B_PE), 1);
         mbar_init(BAR(C::B_DONE), 1);
         *abort_flag = 0;
@@ -329,10 +334,27 @@ __global__ void __launch_bounds__(192, 1)
                           kDrainLimitCycles);
     } else {
         // ------------------------------------------------------------ softmax warps
-        const int q4 = warp & 3;           // this warp's TMEM lane quarter
+        // Warps 2-9: warp w takes TMEM lane quarter w % 4 (its 32 query rows)
+        // and half hf of the columns -- S columns [hf*BN/2, +BN/2), O / head
+        // dims [hf*HD/2, +HD/2).  The two warps of a quarter exchange row
+        // maxima (and at an item's end row sums) through shared memory under a
+        // 64-thread named barrier; exchange buffers alternate, so one barrier
+        // per exchange keeps a write from overtaking the partner's read.
+        constexpr int SW = BN / 2, HW = HD / 2;
+        const int q4 = warp & 3;
+        const int hf = (warp - 2) >> 2;
         const int r = q4 * 32 + lane;      // query row of the tile = TMEM lane
         const int j = r / G, h = r % G;    // token of the tile, head within the kv group
         const uint32_t lane_addr = static_cast<uint32_t>(q4 * 32) << 16;
+        float* xch = reinterpret_cast<float*>(base + C::OFF_XCH);  // [2 buffers][2 halves][128]
+        int xu = 0;
+        auto exchange = [&](float mine) {  // the partner warp's value for this row
+            float* buf = xch + (xu & 1) * 256;
+            ++xu;
+            buf[hf * 128 + r] = mine;
+            named_bar_sync(1 + q4, 64);
+            return buf[(hf ^ 1) * 128 + r];
+        };
         int g = 0, itc = 0;
         for (int it = blockIdx.x; it < a.n_items; it += P, ++itc) {
             const PrefillTile tl = a.tiles[it];
@@ -340,36 +362,39 @@ __global__ void __launch_bounds__(192, 1)
             const int hi_r = live ? tl.tok_row0 + j : -1;
             const int lo_r = live ? (tl.window > 0 ? max(tl.row0, hi_r - tl.window + 1) : tl.row0) : 0;
             const long long io = static_cast<long long>(tl.io0) + static_cast<long long>(j) * tl.io_step;
-            // ---- Q: rotate, split into hi / lo, stage (swizzled, K-major)
+            // ---- Q: rotate this warp's half of the row, split into hi / lo, stage
             if (itc > 0) WAIT(C::B_QE, (itc - 1) & 1, 30, itc);
             float unscale = 1.0f;
             {
-                float qr[HD];
+                float qr[HW];
                 float mx = 0.0f;
                 const float* qin = a.q + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD;
                 const float2* cs = a.rope + static_cast<long long>(tl.rope_row0 + j) * (HD / 2);
 #pragma unroll
-                for (int d = 0; d < HD; ++d) {
-                    qr[d] = live ? rope_elem(qin, d, tl.rope_half, cs, a.neox != 0) : 0.0f;
+                for (int d = 0; d < HW; ++d) {
+                    qr[d] = live ? rope_elem(qin, hf * HW + d, tl.rope_half, cs, a.neox != 0) : 0.0f;
                     mx = fmaxf(mx, fabsf(qr[d]));
                 }
                 float up = 1.0f;
                 if constexpr (DT == DT_F16T) {
+                    mx = fmaxf(mx, exchange(mx));  // the whole row's largest |q|
                     const int e = static_cast<int>((__float_as_uint(mx) >> 23) & 0xFFu) - 127;
                     const int sh = min(60, max(-60, 14 - e));
                     up = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
                     unscale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
                 }
 #pragma unroll
-                for (int c = 0; c < HD / 8; ++c) {
-                    uint32_t hw[4], lw[4];
+                for (int cc = 0; cc < HW / 8; ++cc) {
+                    const int c = hf * (HW / 8) + cc;  // 16-byte chunk of the row
+                    uint32_t hw4[4], lw4[4];
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
-                        split_pair<DT>(qr[8 * c + 2 * i] * up, qr[8 * c + 2 * i + 1] * up, hw[i], lw[i]);
+                        split_pair<DT>(qr[8 * cc + 2 * i] * up, qr[8 * cc + 2 * i + 1] * up, hw4[i],
+                                       lw4[i]);
                     const int off = C::OFF_Q + (c / 8) * C::QSLAB + r * 128 + (((c % 8) ^ (r & 7)) * 16);
-                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
                     *reinterpret_cast<uint4*>(base + off + C::QPART) =
-                        make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                        make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
                 }
             }
             fence_proxy_async_shared();  // generic writes -> tensor-core reads
@@ -377,19 +402,19 @@ __global__ void __launch_bounds__(192, 1)
             if (lane == 0) mbar_arrive(BAR(C::B_QF));
 
             float m = -INFINITY, l = 0.0f, alpha_pend = 0.0f;
-            float o[HD];
+            float o[HW];
 #pragma unroll
-            for (int d = 0; d < HD; ++d) o[d] = 0.0f;
-            // folds tile gg's O (relative to its running max) into o
+            for (int d = 0; d < HW; ++d) o[d] = 0.0f;
+            // folds this warp's half of tile gg's O (relative to its running max) into o
             auto add_o = [&](int gg, float alpha) {
                 const int ob = gg & 1;
                 WAIT(C::B_OF + ob, (gg >> 1) & 1, 31, gg);
                 __syncwarp();  // converged for the .sync.aligned loads
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < HD; c += 32) {
+                for (int c = 0; c < HW; c += 32) {
                     uint32_t t32[32];
-                    tmem_ld32(tmem + lane_addr + C::COL_O + ob * HD + c, t32);
+                    tmem_ld32(tmem + lane_addr + C::COL_O + ob * HD + hf * HW + c, t32);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, __uint_as_float(t32[i]));
                 }
@@ -398,67 +423,88 @@ __global__ void __launch_bounds__(192, 1)
                 if (lane == 0) mbar_arrive(BAR(C::B_OE + ob));
             };
             const int n = tl.n_tiles;
+            // unscale is a power of two: (S * unscale) * scale rounds once, as
+            // the reference's dot * scale does
+            const float sc_mul = a.scale * unscale;
+            const bool capped = a.softcap > 0.0f;
+            // columns every live row of the item attends: [lo_all, hi_all]
+            const int hi_all = tl.tok_row0;  // the first token's row
+            const int lo_all = tl.window > 0
+                                   ? max(tl.row0, tl.tok_row0 + tl.ntok - 1 - tl.window + 1)
+                                   : tl.row0;
             for (int t = 0; t < n; ++t, ++g) {
                 const int sb = g & 1;
                 WAIT(C::B_SF + sb, (g >> 1) & 1, 32, g);
                 __syncwarp();  // converged for the .sync.aligned load
                 tc_fence_after();
-                uint32_t sr[BN];
-                if constexpr (BN == 128) tmem_ld128(tmem + lane_addr + C::COL_S + sb * BN, sr);
-                else tmem_ld64(tmem + lane_addr + C::COL_S + sb * BN, sr);
+                uint32_t sr[SW];
+                if constexpr (SW == 64) tmem_ld64(tmem + lane_addr + C::COL_S + sb * BN + hf * SW, sr);
+                else tmem_ld32(tmem + lane_addr + C::COL_S + sb * BN + hf * SW, sr);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(BAR(C::B_SE + sb));
-                // scores of this row: scale, soft-cap, causal / window limits
-                const int c0 = tl.kv_lo + t * BN;
-                float mt = -INFINITY;
+                // scores of this row's columns: scale, soft-cap, and -- on tiles
+                // that cross a row's causal or window limit -- each row's [lo, hi]
+                const int c0 = tl.kv_lo + t * BN + hf * SW;
+                const int tile0 = tl.kv_lo + t * BN;
+                const bool masked = tile0 + BN - 1 > hi_all || tile0 < lo_all;
+                float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    float v = __fmul_rn(__uint_as_float(sr[c]) * unscale, a.scale);
-                    if (a.softcap > 0.0f) v = __fmul_rn(a.softcap, tanhf(__fmul_rn(v, a.inv_softcap)));
-                    const int col = c0 + c;
-                    v = (col >= lo_r && col <= hi_r) ? v : -INFINITY;
+                for (int c = 0; c < SW; ++c) {
+                    float v = __fmul_rn(__uint_as_float(sr[c]), sc_mul);
+                    if (capped) v = __fmul_rn(a.softcap, tanhf(__fmul_rn(v, a.inv_softcap)));
+                    if (masked) {
+                        const int col = c0 + c;
+                        v = (col >= lo_r && col <= hi_r) ? v : -INFINITY;
+                    }
                     sr[c] = __float_as_uint(v);
-                    mt = fmaxf(mt, v);
+                    mx4[c & 3] = fmaxf(mx4[c & 3], v);
                 }
+                float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                mt = fmaxf(mt, exchange(mt));  // the row's maximum over both halves
                 const float mn = fmaxf(m, mt);
                 const float alpha = m == -INFINITY ? 0.0f : ex2_approx((m - mn) * kLog2eP);
                 m = mn;
-                // P(g) -> shared memory once P.V of the previous tile has read it
-                if (g >= 1) WAIT(C::B_PE, (g - 1) & 1, 33, g);
-                float ls = 0.0f;
+                // p = exp(s - m) and its hi / lo 16-bit parts, in registers before
+                // waiting for the P buffer (this overlaps the previous P.V)
+                uint32_t hw[SW / 2], lw[SW / 2];
+                float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-                for (int c8 = 0; c8 < BN / 8; ++c8) {
-                    float pv[8];
+                for (int c = 0; c < SW; c += 2) {
+                    const float s0 = __uint_as_float(sr[c]), s1 = __uint_as_float(sr[c + 1]);
+                    const float p0 = s0 == -INFINITY ? 0.0f : ex2_approx((s0 - mn) * kLog2eP);
+                    const float p1 = s1 == -INFINITY ? 0.0f : ex2_approx((s1 - mn) * kLog2eP);
+                    ls4[(c >> 1) & 3] += p0 + p1;
+                    split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
+                }
+                const float ls = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+                if (g >= 1) WAIT(C::B_PE, (g - 1) & 1, 33, g);  // P.V of the previous tile read P
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float s = __uint_as_float(sr[8 * c8 + i]);
-                        pv[i] = s == -INFINITY ? 0.0f : ex2_approx((s - mn) * kLog2eP);
-                        ls += pv[i];
-                    }
-                    uint32_t hw[4], lw[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) split_pair<DT>(pv[2 * i], pv[2 * i + 1], hw[i], lw[i]);
+                for (int cc = 0; cc < SW / 8; ++cc) {
+                    const int c8 = hf * (SW / 8) + cc;
                     const int off =
                         C::OFF_P + (c8 / 8) * C::PSLAB + r * 128 + (((c8 % 8) ^ (r & 7)) * 16);
-                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(base + off) =
+                        make_uint4(hw[4 * cc], hw[4 * cc + 1], hw[4 * cc + 2], hw[4 * cc + 3]);
                     *reinterpret_cast<uint4*>(base + off + C::PPART) =
-                        make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                        make_uint4(lw[4 * cc], lw[4 * cc + 1], lw[4 * cc + 2], lw[4 * cc + 3]);
                 }
                 fence_proxy_async_shared();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(BAR(C::B_PF));
-                l = l * alpha + ls;
+                l = l * alpha + ls;  // this half's columns (alpha is the same in both halves)
                 if (t >= 1) add_o(g - 1, alpha_pend);
                 alpha_pend = alpha;
             }
             if (n > 0) add_o(g - 1, alpha_pend);
-            // ---- output row: o / l
-            if (live && l > 0.0f) {
-                const float inv = 1.0f / l;
-                float* dst = a.out + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD;
+            // ---- this half of the output row: o / (l of both halves)
+            const float lt = l + exchange(l);
+            if (live && lt > 0.0f) {
+                const float inv = 1.0f / lt;
+                float* dst = a.out + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD +
+                             hf * HW;
 #pragma unroll
-                for (int d = 0; d < HD; d += 4)
+                for (int d = 0; d < HW; d += 4)
                     *reinterpret_cast<float4*>(dst + d) =
                         make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
             }
@@ -490,7 +536,7 @@ cudaError_t launch_one(const PrefillArgs& a, const CUtensorMap* tk, const CUtens
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    prefill_tc_kernel<HD, DT, G><<<grid, 192, smem, st>>>(*tk, *tv, a);
+    prefill_tc_kernel<HD, DT, G><<<grid, kPfThreads, smem, st>>>(*tk, *tv, a);
     return cudaGetLastError();
 }
 
