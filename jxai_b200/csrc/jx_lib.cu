@@ -316,14 +316,21 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+// A plan buffer in device memory with a ring of pinned host staging buffers:
+// a decode loop whose positions change every step uploads a new plan per
+// call, and a staging buffer is reused only once the copy that last read it
+// has run -- kStaging calls back -- so the host runs ahead of the GPU instead
+// of waiting for the previous step's copy.
+constexpr int kStaging = 4;
 struct PlanSlot {
     std::vector<unsigned char> cached;  // bytes last uploaded
     void* d_buf = nullptr;
     size_t d_cap = 0;
-    void* h_buf = nullptr;  // pinned staging
-    size_t h_cap = 0;
-    cudaEvent_t ev = nullptr;
-    bool ev_pending = false;
+    void* h_buf[kStaging] = {};  // pinned staging
+    size_t h_cap[kStaging] = {};
+    cudaEvent_t ev[kStaging] = {};
+    bool ev_pending[kStaging] = {};
+    int next = 0;
 };
 
 }  // namespace
@@ -449,25 +456,27 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
             return fail(JX_ERR_NOMEM, "plan buffer allocation of %zu bytes failed", cap);
         s.d_cap = cap;
     }
-    if (!s.ev) JX_CUDA(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming));
-    if (s.ev_pending) {
-        JX_CUDA(cudaEventSynchronize(s.ev));
-        s.ev_pending = false;
+    const int b = s.next;
+    s.next = (b + 1) % kStaging;
+    if (!s.ev[b]) JX_CUDA(cudaEventCreateWithFlags(&s.ev[b], cudaEventDisableTiming));
+    if (s.ev_pending[b]) {
+        JX_CUDA(cudaEventSynchronize(s.ev[b]));
+        s.ev_pending[b] = false;
     }
-    if (s.h_cap < bytes.size()) {
-        if (s.h_buf) JX_CUDA(cudaFreeHost(s.h_buf));
-        s.h_buf = nullptr;
-        s.h_cap = 0;
+    if (s.h_cap[b] < bytes.size()) {
+        if (s.h_buf[b]) JX_CUDA(cudaFreeHost(s.h_buf[b]));
+        s.h_buf[b] = nullptr;
+        s.h_cap[b] = 0;
         const size_t cap = std::max<size_t>(bytes.size() * 2, 4096);
-        if (cudaHostAlloc(&s.h_buf, cap, cudaHostAllocDefault) != cudaSuccess)
+        if (cudaHostAlloc(&s.h_buf[b], cap, cudaHostAllocDefault) != cudaSuccess)
             return fail(JX_ERR_NOMEM, "pinned staging allocation of %zu bytes failed", cap);
-        s.h_cap = cap;
+        s.h_cap[b] = cap;
     }
-    std::memcpy(s.h_buf, bytes.data(), bytes.size());
+    std::memcpy(s.h_buf[b], bytes.data(), bytes.size());
     ++kv->generation;
-    JX_CUDA(cudaMemcpyAsync(s.d_buf, s.h_buf, bytes.size(), cudaMemcpyHostToDevice, stream));
-    JX_CUDA(cudaEventRecord(s.ev, stream));
-    s.ev_pending = true;
+    JX_CUDA(cudaMemcpyAsync(s.d_buf, s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice, stream));
+    JX_CUDA(cudaEventRecord(s.ev[b], stream));
+    s.ev_pending[b] = true;
     s.cached = bytes;
     return JX_OK;
 }
@@ -1481,9 +1490,11 @@ int jx_kv_destroy(jx_kv* kv) {
     if (kv->ev_t0) cudaEventDestroy(kv->ev_t0);
     if (kv->ev_t1) cudaEventDestroy(kv->ev_t1);
     for (PlanSlot& s : kv->slots) {
-        if (s.ev) cudaEventDestroy(s.ev);
+        for (int b = 0; b < kStaging; ++b) {
+            if (s.ev[b]) cudaEventDestroy(s.ev[b]);
+            if (s.h_buf[b]) cudaFreeHost(s.h_buf[b]);
+        }
         cudaFree(s.d_buf);
-        if (s.h_buf) cudaFreeHost(s.h_buf);
     }
     delete kv;
     return JX_OK;

@@ -41,7 +41,9 @@ namespace {
 
 constexpr float kLog2eP = 1.4426950408889634f;
 constexpr int kSoftmaxWarps = 8;                       // warps 2-9
-constexpr int kPfThreads = 32 * (2 + kSoftmaxWarps);   // + TMA warp, MMA warp
+// + TMA warp, MMA warp.  Ten warps put three on two of the SM's four
+// sub-partitions (16K registers each): at most 170 registers per thread.
+constexpr int kPfThreads = 32 * (2 + kSoftmaxWarps);
 
 // Loads 32 consecutive 32-bit TMEM columns of this thread's lane and waits
 // for them (one asm statement: the registers are valid when it ends).
@@ -366,15 +368,61 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             if (itc > 0) WAIT(C::B_QE, (itc - 1) & 1, 30, itc);
             float unscale = 1.0f;
             {
-                float qr[HW];
-                float mx = 0.0f;
+                // rotation of this warp's half of the row (dims [hf*HW, +HW)),
+                // 8 dims at a time: each batch's operands are loaded together
+                // (independent loads in flight), then rotated with the rounding
+                // forms of rope_elem -- Neox pairs (j, j + HD/2), which for full
+                // rotary put half 0 at j = d and half 1 at j = d - HD/2;
+                // interleaved pairs (2j, 2j + 1) within the half
                 const float* qin = a.q + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD;
                 const float2* cs = a.rope + static_cast<long long>(tl.rope_row0 + j) * (HD / 2);
+                float qr[HW];
+                float mx = 0.0f;
+                if (!live) {
 #pragma unroll
-                for (int d = 0; d < HW; ++d) {
-                    qr[d] = live ? rope_elem(qin, hf * HW + d, tl.rope_half, cs, a.neox != 0) : 0.0f;
-                    mx = fmaxf(mx, fabsf(qr[d]));
+                    for (int dd = 0; dd < HW; ++dd) qr[dd] = 0.0f;
+                } else if (tl.rope_half == HD / 2 && a.neox) {
+#pragma unroll
+                    for (int b0 = 0; b0 < HW; b0 += 8) {
+                        float xa[8], xb[8];
+                        float2 c[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            xa[i] = __ldg(qin + b0 + i);
+                            xb[i] = __ldg(qin + HD / 2 + b0 + i);
+                            c[i] = __ldg(cs + b0 + i);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            qr[b0 + i] = hf == 0 ? __fmaf_rn(xa[i], c[i].x, -__fmul_rn(xb[i], c[i].y))
+                                                 : __fmaf_rn(xa[i], c[i].y, __fmul_rn(xb[i], c[i].x));
+                    }
+                } else if (tl.rope_half == HD / 2) {
+#pragma unroll
+                    for (int b0 = 0; b0 < HW; b0 += 8) {
+                        const int d0 = hf * HW + b0;
+                        float x[8];
+                        float2 c[4];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) x[i] = __ldg(qin + d0 + i);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) c[i] = __ldg(cs + d0 / 2 + i);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float aa = x[i & ~1], bb = x[i | 1];
+                            const float2 t = c[i >> 1];
+                            qr[b0 + i] = (i & 1) == 0 ? __fsub_rn(__fmul_rn(aa, t.x), __fmul_rn(bb, t.y))
+                                                      : __fadd_rn(__fmul_rn(aa, t.y), __fmul_rn(bb, t.x));
+                        }
+                    }
+                } else {
+                    // partial rotary
+#pragma unroll
+                    for (int dd = 0; dd < HW; ++dd)
+                        qr[dd] = rope_elem(qin, hf * HW + dd, tl.rope_half, cs, a.neox != 0);
                 }
+#pragma unroll
+                for (int dd = 0; dd < HW; ++dd) mx = fmaxf(mx, fabsf(qr[dd]));
                 float up = 1.0f;
                 if constexpr (DT == DT_F16T) {
                     mx = fmaxf(mx, exchange(mx));  // the whole row's largest |q|
@@ -449,16 +497,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int tile0 = tl.kv_lo + t * BN;
                 const bool masked = tile0 + BN - 1 > hi_all || tile0 < lo_all;
                 float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (!capped && !masked) {
 #pragma unroll
-                for (int c = 0; c < SW; ++c) {
-                    float v = __fmul_rn(__uint_as_float(sr[c]), sc_mul);
-                    if (capped) v = __fmul_rn(a.softcap, tanhf(__fmul_rn(v, a.inv_softcap)));
-                    if (masked) {
-                        const int col = c0 + c;
-                        v = (col >= lo_r && col <= hi_r) ? v : -INFINITY;
+                    for (int c = 0; c < SW; ++c) {
+                        const float v = __fmul_rn(__uint_as_float(sr[c]), sc_mul);
+                        sr[c] = __float_as_uint(v);
+                        mx4[c & 3] = fmaxf(mx4[c & 3], v);
                     }
-                    sr[c] = __float_as_uint(v);
-                    mx4[c & 3] = fmaxf(mx4[c & 3], v);
+                } else {
+#pragma unroll
+                    for (int c = 0; c < SW; ++c) {
+                        float v = __fmul_rn(__uint_as_float(sr[c]), sc_mul);
+                        if (capped) v = __fmul_rn(a.softcap, tanhf(__fmul_rn(v, a.inv_softcap)));
+                        const int col = c0 + c;
+                        if (masked) v = (col >= lo_r && col <= hi_r) ? v : -INFINITY;
+                        sr[c] = __float_as_uint(v);
+                        mx4[c & 3] = fmaxf(mx4[c & 3], v);
+                    }
                 }
                 float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                 mt = fmaxf(mt, exchange(mt));  // the row's maximum over both halves
@@ -466,16 +521,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const float alpha = m == -INFINITY ? 0.0f : ex2_approx((m - mn) * kLog2eP);
                 m = mn;
                 // p = exp(s - m) and its hi / lo 16-bit parts, in registers before
-                // waiting for the P buffer (this overlaps the previous P.V)
+                // waiting for the P buffer (this overlaps the previous P.V).
+                // ex2(-inf) is +0, so masked columns need no test once the max is
+                // finite (a row with no attended column yet uses 0).
+                const float mref = mn == -INFINITY ? 0.0f : mn;
                 uint32_t hw[SW / 2], lw[SW / 2];
                 float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < SW; c += 2) {
-                    const float s0 = __uint_as_float(sr[c]), s1 = __uint_as_float(sr[c + 1]);
-                    const float p0 = s0 == -INFINITY ? 0.0f : ex2_approx((s0 - mn) * kLog2eP);
-                    const float p1 = s1 == -INFINITY ? 0.0f : ex2_approx((s1 - mn) * kLog2eP);
+                    const float p0 = ex2_approx((__uint_as_float(sr[c]) - mref) * kLog2eP);
+                    const float p1 = ex2_approx((__uint_as_float(sr[c + 1]) - mref) * kLog2eP);
                     ls4[(c >> 1) & 3] += p0 + p1;
-                    split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
+                    if constexpr (DT == DT_BF16) {
+                        // hi: p truncated to bf16 (exact bit mask); lo = p - hi
+                        // (exact) rounded to nearest: p to ~2^-16 relative, one
+                        // conversion per pair
+                        const uint32_t b0 = __float_as_uint(p0) & 0xFFFF0000u;
+                        const uint32_t b1 = __float_as_uint(p1) & 0xFFFF0000u;
+                        hw[c / 2] = __byte_perm(b0, b1, 0x7632);
+                        asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
+                            : "=r"(lw[c / 2])
+                            : "f"(p1 - __uint_as_float(b1)), "f"(p0 - __uint_as_float(b0)));
+                    } else {
+                        split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
+                    }
                 }
                 const float ls = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
                 if (g >= 1) WAIT(C::B_PE, (g - 1) & 1, 33, g);  // P.V of the previous tile read P
