@@ -120,6 +120,7 @@ struct PrefillArgs {
     const PrefillTile* tiles;
     int n_items;
     int neox;
+    int q_vec;  // 1: q rows start 16-byte aligned (16-byte loads)
     const float* q;
     float* out;
     long long q_stride;

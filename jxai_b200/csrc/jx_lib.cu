@@ -761,6 +761,7 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
     pa.tiles = static_cast<const PrefillTile*>(kv->slots[slot].d_buf);
     pa.n_items = static_cast<int>(items.size());
     pa.neox = neox ? 1 : 0;
+    pa.q_vec = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
     pa.q = a->q;
     pa.out = a->out;
     pa.q_stride = a->q_stride;

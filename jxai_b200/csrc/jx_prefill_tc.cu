@@ -137,6 +137,10 @@ __host__ __device__ constexpr uint32_t idesc_f16(int dt, int M, int N, bool b_mn
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+__device__ __forceinline__ float f4_at(const float4& v, int i) {
+    return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
 template <int HD>
 struct PfCfg {
     static constexpr int BN = HD == 64 ? 128 : 64;  // cache rows per K/V tile
@@ -226,6 +230,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         int g = 0, n_issued = 0;
         for (int it = blockIdx.x; it < a.n_items; it += P) {
             const PrefillTile tl = a.tiles[it];
+            if (it + P < a.n_items) {
+                // the next item's 128 q rows and their (cos, sin) rows into L2
+                // (this warp is idle most of the time): its Q staging then
+                // reads L2, not DRAM
+                const PrefillTile nx = a.tiles[it + P];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int r = lane * 4 + k, jj = r / G, hh = r % G;
+                    if (jj < nx.ntok) {
+                        const char* qrow = reinterpret_cast<const char*>(
+                            a.q + (static_cast<long long>(nx.io0) + static_cast<long long>(jj) * nx.io_step) *
+                                      a.q_stride +
+                            static_cast<long long>(nx.kvh * G + hh) * HD);
+                        const char* crow = reinterpret_cast<const char*>(
+                            a.rope + static_cast<long long>(nx.rope_row0 + jj) * (HD / 2));
+#pragma unroll
+                        for (int b = 0; b < HD * 4; b += 128) {
+                            asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + b));
+                            asm volatile("prefetch.global.L2 [%0];" ::"l"(crow + b));
+                        }
+                    }
+                }
+            }
             for (int t = 0; t < tl.n_tiles; ++t, ++g) {
                 const int st = g % C::NS;
                 if (g >= C::NS) WAIT(C::B_KVE + st, ((g / C::NS) & 1) ^ 1u, 21, g);
@@ -369,7 +396,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             float unscale = 1.0f;
             {
                 // rotation of this warp's half of the row (dims [hf*HW, +HW)),
-                // 8 dims at a time: each batch's operands are loaded together
+                // 16 dims at a time: each batch's operands are loaded together
                 // (independent loads in flight), then rotated with the rounding
                 // forms of rope_elem -- Neox pairs (j, j + HD/2), which for full
                 // rotary put half 0 at j = d and half 1 at j = d - HD/2;
@@ -381,34 +408,81 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (!live) {
 #pragma unroll
                     for (int dd = 0; dd < HW; ++dd) qr[dd] = 0.0f;
+                } else if (tl.rope_half == HD / 2 && a.q_vec) {
+                    // 16-byte loads: every lane reads its own row, so each
+                    // warp-wide load touches 32 lines -- a quarter as many
+                    // requests as 4-byte loads
+                    const float4* q4 = reinterpret_cast<const float4*>(qin);
+                    const float4* c4 = reinterpret_cast<const float4*>(cs);  // 2 (cos, sin) pairs each
+                    if (a.neox) {
+#pragma unroll
+                        for (int b0 = 0; b0 < HW; b0 += 16) {
+                            float4 xa[4], xb[4], cc[8];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                xa[i] = __ldg(q4 + b0 / 4 + i);
+                                xb[i] = __ldg(q4 + (HD / 2 + b0) / 4 + i);
+                            }
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) cc[i] = __ldg(c4 + b0 / 2 + i);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float va = f4_at(xa[i / 4], i % 4), vb = f4_at(xb[i / 4], i % 4);
+                                const float cx = (i & 1) ? cc[i / 2].z : cc[i / 2].x;
+                                const float sy = (i & 1) ? cc[i / 2].w : cc[i / 2].y;
+                                qr[b0 + i] = hf == 0 ? __fmaf_rn(va, cx, -__fmul_rn(vb, sy))
+                                                     : __fmaf_rn(va, sy, __fmul_rn(vb, cx));
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int b0 = 0; b0 < HW; b0 += 16) {
+                            const int d0 = hf * HW + b0;
+                            float4 x4[4], cc[4];
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) x4[i] = __ldg(q4 + d0 / 4 + i);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) cc[i] = __ldg(c4 + d0 / 4 + i);
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                const float aa = f4_at(x4[i / 4], i % 4 & ~1);
+                                const float bb = f4_at(x4[i / 4], (i % 4) | 1);
+                                // pair i/2 -> (cos, sin) entry i/2: float4 i/4, half (i/2) & 1
+                                const float cx = ((i / 2) & 1) ? cc[i / 4].z : cc[i / 4].x;
+                                const float sy = ((i / 2) & 1) ? cc[i / 4].w : cc[i / 4].y;
+                                qr[b0 + i] = (i & 1) == 0 ? __fsub_rn(__fmul_rn(aa, cx), __fmul_rn(bb, sy))
+                                                          : __fadd_rn(__fmul_rn(aa, sy), __fmul_rn(bb, cx));
+                            }
+                        }
+                    }
                 } else if (tl.rope_half == HD / 2 && a.neox) {
 #pragma unroll
-                    for (int b0 = 0; b0 < HW; b0 += 8) {
-                        float xa[8], xb[8];
-                        float2 c[8];
+                    for (int b0 = 0; b0 < HW; b0 += 16) {
+                        float xa[16], xb[16];
+                        float2 c[16];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                        for (int i = 0; i < 16; ++i) {
                             xa[i] = __ldg(qin + b0 + i);
                             xb[i] = __ldg(qin + HD / 2 + b0 + i);
                             c[i] = __ldg(cs + b0 + i);
                         }
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
+                        for (int i = 0; i < 16; ++i)
                             qr[b0 + i] = hf == 0 ? __fmaf_rn(xa[i], c[i].x, -__fmul_rn(xb[i], c[i].y))
                                                  : __fmaf_rn(xa[i], c[i].y, __fmul_rn(xb[i], c[i].x));
                     }
                 } else if (tl.rope_half == HD / 2) {
 #pragma unroll
-                    for (int b0 = 0; b0 < HW; b0 += 8) {
+                    for (int b0 = 0; b0 < HW; b0 += 16) {
                         const int d0 = hf * HW + b0;
-                        float x[8];
-                        float2 c[4];
+                        float x[16];
+                        float2 c[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) x[i] = __ldg(qin + d0 + i);
+                        for (int i = 0; i < 16; ++i) x[i] = __ldg(qin + d0 + i);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) c[i] = __ldg(cs + d0 / 2 + i);
+                        for (int i = 0; i < 8; ++i) c[i] = __ldg(cs + d0 / 2 + i);
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                        for (int i = 0; i < 16; ++i) {
                             const float aa = x[i & ~1], bb = x[i | 1];
                             const float2 t = c[i >> 1];
                             qr[b0 + i] = (i & 1) == 0 ? __fsub_rn(__fmul_rn(aa, t.x), __fmul_rn(bb, t.y))
@@ -534,14 +608,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     ls4[(c >> 1) & 3] += p0 + p1;
                     if constexpr (DT == DT_BF16) {
                         // hi: p truncated to bf16 (exact bit mask); lo = p - hi
-                        // (exact) rounded to nearest: p to ~2^-16 relative, one
-                        // conversion per pair
+                        // (exact), rounded to the nearest bf16 by adding half
+                        // an ulp to its bits (ties away from zero: the same
+                        // half-ulp bound as ties to even) -- integer work that
+                        // leaves the special-function pipe to ex2
                         const uint32_t b0 = __float_as_uint(p0) & 0xFFFF0000u;
                         const uint32_t b1 = __float_as_uint(p1) & 0xFFFF0000u;
                         hw[c / 2] = __byte_perm(b0, b1, 0x7632);
-                        asm("cvt.rn.bf16x2.f32 %0, %1, %2;"
-                            : "=r"(lw[c / 2])
-                            : "f"(p1 - __uint_as_float(b1)), "f"(p0 - __uint_as_float(b0)));
+                        const uint32_t r0 = __float_as_uint(p0 - __uint_as_float(b0)) + 0x8000u;
+                        const uint32_t r1 = __float_as_uint(p1 - __uint_as_float(b1)) + 0x8000u;
+                        lw[c / 2] = __byte_perm(r0, r1, 0x7632);
                     } else {
                         split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
                     }
