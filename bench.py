@@ -33,10 +33,31 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+    # NCCL's communicator lines (rank, nRanks, transports) in the run's
+    # output (on stderr: main() keeps stdout for the JSON line).  Set before
+    # torch (and its NCCL) is loaded, which reads them once; a level below
+    # INFO (an environment's VERSION or WARN) is raised, INFO / TRACE kept.
+    if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+
 from jxai_b200 import workloads as W  # noqa: E402
 
 METRIC = "decode-attn KV-read HBM GB/s"
 FALLBACK_HBM_GBS = 6650.0
+_JSON_FD = None  # the process's original stdout when fd 1 was sent to stderr
+
+
+def emit(line: dict) -> None:
+    """Prints the run's one JSON line on the original standard output."""
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        sys.stdout.write(text)
+        sys.stdout.flush()
+    else:
+        sys.stdout.flush()
+        os.write(_JSON_FD, text.encode())
 
 
 def parse_args():
@@ -497,7 +518,7 @@ def run_ours(args, rank, world, local_rank):
         "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
         "gpu_launches": int(r.launches_per_step() * K),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------------- CPU side
@@ -624,7 +645,7 @@ def run_reference(args, rank, world):
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def _engine_driver() -> str:
@@ -689,7 +710,7 @@ def run_engine(args, rank, world):
         "staging": res, "cpu_baseline": cpu,
         "kv_gbs": round(w.kv_read_bytes() / (best["ms_per_token"] * 1e-3) / 1e9, 2),
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def run_prefill(args, rank, world):
@@ -795,7 +816,7 @@ def run_prefill(args, rank, world):
                             "causal attention; 8/G consecutive tokens share a pass over their rows)"),
         "gpu_launches": launches * K, "cpu_baseline": cpu,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def main():
@@ -815,11 +836,13 @@ def main():
     import torch
     import torch.distributed as dist
     if world > 1:
-        # NCCL's communicator lines (rank, nranks, transports) go to stderr:
-        # stdout keeps the one JSON line
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        # stdout must hold the one JSON line: file descriptor 1 goes to
+        # stderr for the whole run (NCCL's communicator lines, libraries and
+        # prints alike) and the JSON line is written to the saved stdout
+        global _JSON_FD
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
         from datetime import timedelta
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),

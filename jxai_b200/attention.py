@@ -333,7 +333,8 @@ def attn_step_sharded(cache: KVCache, layers: Sequence[Layer], q, k, v, out, pos
                       n_heads: int, n_kv_heads: int, comm, timeout_ms: int = 0,
                       scale: Optional[float] = None, softcap: float = 0.0,
                       sliding_window: int = 0, yarn_scale: float = 1.0, neox: bool = True,
-                      seq_ids: Optional[Sequence[int]] = None, stream=None) -> None:
+                      seq_ids: Optional[Sequence[int]] = None, stream=None, heartbeat=None,
+                      step: int = 0, liveness_timeout_s: float = 5.0) -> None:
     """One context sharded by position over the ranks of an NCCL communicator.
 
     This rank's cache holds positions [pos_base, pos_base + capacity); the call
