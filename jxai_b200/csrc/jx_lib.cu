@@ -316,20 +316,30 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// A plan buffer in device memory with a ring of pinned host staging buffers:
-// a decode loop whose positions change every step uploads a new plan per
-// call, and a staging buffer is reused only once the copy that last read it
-// has run -- kStaging calls back -- so the host runs ahead of the GPU instead
-// of waiting for the previous step's copy.
+// A work plan in device memory.  A decode loop whose positions change every
+// step uploads a new plan per call: plans go to a ring of kStaging device
+// buffers, each filled from its own pinned host buffer by a copy on a side
+// stream, and the step's stream waits only for that copy's event.  The
+// step's stream thus runs staging kernel -> decode kernel with no copy-engine
+// operation between them (which cost ~25 us of GPU time per step), and the
+// host runs up to kStaging calls ahead.  A ring buffer is refilled only after
+// the launches that last read it (ev_used) and the copy that last read its
+// host buffer (ev_copy) are done.  While a stream is being captured into a
+// graph, the copy stays on that stream (a captured stream cannot wait for an
+// uncaptured one).
 constexpr int kStaging = 4;
 struct PlanSlot {
     std::vector<unsigned char> cached;  // bytes last uploaded
-    void* d_buf = nullptr;
-    size_t d_cap = 0;
+    void* d_buf = nullptr;              // the buffer holding `cached`
+    int cur = -1;                       // its ring index
+    void* d_ring[kStaging] = {};
+    size_t d_cap[kStaging] = {};
     void* h_buf[kStaging] = {};  // pinned staging
     size_t h_cap[kStaging] = {};
-    cudaEvent_t ev[kStaging] = {};
-    bool ev_pending[kStaging] = {};
+    cudaEvent_t ev_copy[kStaging] = {};
+    bool copy_pending[kStaging] = {};
+    cudaEvent_t ev_used[kStaging] = {};
+    bool used_pending[kStaging] = {};
     int next = 0;
 };
 
@@ -384,6 +394,18 @@ struct jx_kv {
     // device copies of a step's host-resident q/k/v (stage_host_inputs)
     float* d_stage = nullptr;
     size_t stage_floats = 0;
+    cudaStream_t up_stream = nullptr;  // plan copies (upload_plan)
+    // copies of host-resident q/k/v decided by stage_host_inputs, launched by
+    // the step right before its first kernel (after its plan uploads)
+    struct PendingStage {
+        bool active = false;
+        const float* src[3] = {};
+        float* dst[3] = {};
+        long long n[3] = {};
+        int grid = 0;
+    } pend;
+    std::vector<int> used_slots;       // plan slots the current call's launches read
+    std::vector<int> replay_slots;     // plan slots the recorded launches read
 };
 
 namespace {
@@ -446,22 +468,25 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
                 cudaStream_t stream) {
     if (kv->slots.size() <= slot_i) kv->slots.resize(slot_i + 1);
     PlanSlot& s = kv->slots[slot_i];
+    kv->used_slots.push_back(static_cast<int>(slot_i));
     if (s.cached == bytes && s.d_buf) return JX_OK;
-    if (s.d_cap < bytes.size()) {
-        if (s.d_buf) JX_CUDA(cudaFree(s.d_buf));
-        s.d_buf = nullptr;
-        s.d_cap = 0;
-        const size_t cap = std::max<size_t>(bytes.size() * 2, 4096);
-        if (cudaMalloc(&s.d_buf, cap) != cudaSuccess)
-            return fail(JX_ERR_NOMEM, "plan buffer allocation of %zu bytes failed", cap);
-        s.d_cap = cap;
-    }
     const int b = s.next;
     s.next = (b + 1) % kStaging;
-    if (!s.ev[b]) JX_CUDA(cudaEventCreateWithFlags(&s.ev[b], cudaEventDisableTiming));
-    if (s.ev_pending[b]) {
-        JX_CUDA(cudaEventSynchronize(s.ev[b]));
-        s.ev_pending[b] = false;
+    if (s.d_cap[b] < bytes.size()) {
+        if (s.d_ring[b]) JX_CUDA(cudaFree(s.d_ring[b]));  // (synchronises the device)
+        s.d_ring[b] = nullptr;
+        s.d_cap[b] = 0;
+        s.used_pending[b] = false;
+        const size_t cap = std::max<size_t>(bytes.size() * 2, 4096);
+        if (cudaMalloc(&s.d_ring[b], cap) != cudaSuccess)
+            return fail(JX_ERR_NOMEM, "plan buffer allocation of %zu bytes failed", cap);
+        s.d_cap[b] = cap;
+    }
+    if (!s.ev_copy[b]) JX_CUDA(cudaEventCreateWithFlags(&s.ev_copy[b], cudaEventDisableTiming));
+    if (!s.ev_used[b]) JX_CUDA(cudaEventCreateWithFlags(&s.ev_used[b], cudaEventDisableTiming));
+    if (s.copy_pending[b]) {
+        JX_CUDA(cudaEventSynchronize(s.ev_copy[b]));  // the host buffer's previous copy ran
+        s.copy_pending[b] = false;
     }
     if (s.h_cap[b] < bytes.size()) {
         if (s.h_buf[b]) JX_CUDA(cudaFreeHost(s.h_buf[b]));
@@ -474,10 +499,52 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
     }
     std::memcpy(s.h_buf[b], bytes.data(), bytes.size());
     ++kv->generation;
-    JX_CUDA(cudaMemcpyAsync(s.d_buf, s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice, stream));
-    JX_CUDA(cudaEventRecord(s.ev[b], stream));
-    s.ev_pending[b] = true;
+    cudaStreamCaptureStatus cap_st = cudaStreamCaptureStatusNone;
+    JX_CUDA(cudaStreamIsCapturing(stream, &cap_st));
+    if (cap_st != cudaStreamCaptureStatusNone) {
+        // captured: the copy is a node of the stream's graph
+        JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
+                                stream));
+    } else {
+        if (!kv->up_stream)
+            JX_CUDA(cudaStreamCreateWithFlags(&kv->up_stream, cudaStreamNonBlocking));
+        if (s.used_pending[b]) JX_CUDA(cudaStreamWaitEvent(kv->up_stream, s.ev_used[b], 0));
+        JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
+                                kv->up_stream));
+        JX_CUDA(cudaEventRecord(s.ev_copy[b], kv->up_stream));
+        s.copy_pending[b] = true;
+        JX_CUDA(cudaStreamWaitEvent(stream, s.ev_copy[b], 0));
+    }
+    s.d_buf = s.d_ring[b];
+    s.cur = b;
     s.cached = bytes;
+    return JX_OK;
+}
+
+// Launches the copies of host-resident step inputs that stage_host_inputs
+// decided on, once per call, before the call's first kernel: after the plan
+// uploads, so that no stream wait separates the staging kernel from the
+// launch it feeds.
+int flush_staging(jx_kv* kv, cudaStream_t stream) {
+    if (!kv->pend.active) return JX_OK;
+    auto& p = kv->pend;
+    p.active = false;
+    stage_inputs_kernel<<<p.grid, 256, 0, stream>>>(p.src[0], p.dst[0], p.n[0], p.src[1], p.dst[1],
+                                                    p.n[1], p.src[2], p.dst[2], p.n[2]);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(JX_ERR_CUDA, "input staging launch: %s", cudaGetErrorString(e));
+    return JX_OK;
+}
+
+// After a call's launches: each plan buffer they read is marked as read up
+// to this point of `stream` (upload_plan refills it only after that).
+int mark_plans_used(jx_kv* kv, const std::vector<int>& slots, cudaStream_t stream) {
+    for (int si : slots) {
+        PlanSlot& s = kv->slots[static_cast<size_t>(si)];
+        if (s.cur < 0) continue;
+        JX_CUDA(cudaEventRecord(s.ev_used[s.cur], stream));
+        s.used_pending[s.cur] = true;
+    }
     return JX_OK;
 }
 
@@ -739,6 +806,8 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
     const size_t slot = gi;
     rc = upload_plan(kv, slot, bytes, stream);
     if (rc) return rc;
+    rc = flush_staging(kv, stream);
+    if (rc) return rc;
     {
         unsigned char* dplan = static_cast<unsigned char*>(kv->slots[slot].d_buf);
         const PairRow* dp = reinterpret_cast<const PairRow*>(dplan + app_off);
@@ -791,14 +860,22 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
     if (!prefill && kv->replay_generation == kv->generation && key == kv->replay_key) {
         DeviceGuard guard(kv->d.device);
         if (!guard.ok) return fail(JX_ERR_CUDA, "cannot select device %d", kv->d.device);
+        {
+            const int rc = flush_staging(kv, stream);
+            if (rc) return rc;
+        }
         for (const DecodeLaunch& Lc : kv->replay) {
             const cudaError_t e = decode_launch(Lc);
             if (e != cudaSuccess)
                 return fail(JX_ERR_CUDA, "decode launch failed: %s", cudaGetErrorString(e));
         }
         kv->last_launches = static_cast<int>(kv->replay.size());
+        cudaStreamCaptureStatus cap_st = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(stream, &cap_st) == cudaSuccess && cap_st == cudaStreamCaptureStatusNone)
+            return mark_plans_used(kv, kv->replay_slots, stream);
         return JX_OK;
     }
+    kv->used_slots.clear();
     kv->replay_generation = ~0ull;
     kv->replay.clear();
     std::vector<DecodeLaunch> launched;
@@ -1127,6 +1204,8 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         }
         rc = upload_plan(kv, gi, bytes, stream);
         if (rc) return rc;
+        rc = flush_staging(kv, stream);
+        if (rc) return rc;
         if (prefill && !pairs.empty()) {
             // all of this group's rows are stored before any of them is attended
             const PairRow* dp = static_cast<const PairRow*>(kv->slots[gi].d_buf);
@@ -1233,9 +1312,22 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
         launched.push_back(Lc);
     }
     kv->last_launches = launches;
+    {
+        const int rc = flush_staging(kv, stream);
+        if (rc) return rc;
+    }
+    {
+        cudaStreamCaptureStatus cap_st = cudaStreamCaptureStatusNone;
+        JX_CUDA(cudaStreamIsCapturing(stream, &cap_st));
+        if (cap_st == cudaStreamCaptureStatusNone) {
+            const int rc = mark_plans_used(kv, kv->used_slots, stream);
+            if (rc) return rc;
+        }
+    }
     if (prefill) return JX_OK;  // not replayed: its append launches are not recorded
     kv->replay_key = std::move(key);
     kv->replay = std::move(launched);
+    kv->replay_slots = kv->used_slots;
     kv->replay_generation = kv->generation;
     return JX_OK;
 }
@@ -1383,10 +1475,16 @@ int stage_host_inputs(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
     const long long work = (host[0] ? n_q : 0) + (host[1] ? 2 * n_kv : 0);
     const int grid = static_cast<int>(std::min<long long>(
         std::max<long long>((work / 4 + 255) / 256, 1), 4ll * std::max(kv->num_sms, 1)));
-    stage_inputs_kernel<<<grid, 256, 0, stream>>>(src[0], dst[0], n_q, src[1], dst[1], n_kv,
-                                                  src[2], dst[2], n_kv);
-    const cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return fail(JX_ERR_CUDA, "input staging launch: %s", cudaGetErrorString(e));
+    // launched by the step (flush_staging) right before its first kernel
+    auto& p = kv->pend;
+    p.active = true;
+    p.grid = grid;
+    const long long nn[3] = {n_q, n_kv, n_kv};
+    for (int b = 0; b < 3; ++b) {
+        p.src[b] = src[b];
+        p.dst[b] = dst[b];
+        p.n[b] = nn[b];
+    }
     if (host[0]) staged->q = dst[0];
     if (host[1]) staged->k = dst[1];
     if (host[2]) staged->v = dst[2];
@@ -1406,6 +1504,7 @@ int timed_step(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const 
     jx_step_args staged{};
     int rc = stage_host_inputs(kv, layers, n_layers, a, stream, &staged);
     if (!rc) rc = step_impl(kv, layers, n_layers, &staged, partials, stream, prefill);
+    kv->pend.active = false;  // a call that failed before its first launch copies nothing
     if (kv->opt_timing) {
         JX_CUDA(cudaEventRecord(kv->ev_t1, stream));
         kv->timed = rc == JX_OK;
@@ -1492,11 +1591,13 @@ int jx_kv_destroy(jx_kv* kv) {
     if (kv->ev_t1) cudaEventDestroy(kv->ev_t1);
     for (PlanSlot& s : kv->slots) {
         for (int b = 0; b < kStaging; ++b) {
-            if (s.ev[b]) cudaEventDestroy(s.ev[b]);
+            if (s.ev_copy[b]) cudaEventDestroy(s.ev_copy[b]);
+            if (s.ev_used[b]) cudaEventDestroy(s.ev_used[b]);
             if (s.h_buf[b]) cudaFreeHost(s.h_buf[b]);
+            cudaFree(s.d_ring[b]);
         }
-        cudaFree(s.d_buf);
     }
+    if (kv->up_stream) cudaStreamDestroy(kv->up_stream);
     delete kv;
     return JX_OK;
 }
