@@ -215,8 +215,9 @@ JX_API int jx_attn_step_sharded(jx_kv* kv, const jx_layer_desc* layers, uint32_t
  * counters, work plan) is one fixed 8 MiB array per GPU, reserved while the
  * library is loaded.  Steps needing more scratch are rejected with
  * JX_ERR_RANGE.  All calls share that array: calls that overlap on the GPU
- * race.  The first call on a device looks up the array's address; make it
- * before any stream capture.  All layers of one call share head_dim, and no
+ * race.  The call cannot be captured into a CUDA graph (it returns
+ * JX_ERR_UNSUPPORTED while its stream is capturing: its plan is copied from
+ * a host slot that later calls reuse).  All layers of one call share head_dim, and no
  * shares_kv layer may read a cache layer appended in the same call. */
 JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache, void* v_cache,
                                 const jx_layer_desc* layers, uint32_t n_layers,

@@ -32,7 +32,8 @@
 //     creates that device's plan-copy events; the first call in the process
 //     also page-locks the fixed host buffer the plan is built in
 //     (cudaHostRegister of the library's own static buffer -- no memory is
-//     allocated).  Make that first call before any stream capture.
+//     allocated).  The call refuses stream capture (JX_ERR_UNSUPPORTED): a
+//     captured plan copy would replay from a slot later calls overwrite.
 //   * Nothing here calls cudaMalloc, cudaFree, cudaMallocAsync, cudaHostAlloc
 //     or any other allocating routine: the work plan is built in one of four
 //     slots of the fixed host buffer (not on the heap) and copied into the
@@ -233,6 +234,16 @@ extern "C" JX_API int jx_attn_step_noalloc(const jx_kv_desc* desc, void* k_cache
     if (!rc) rc = check_ptr(v_cache, "v_cache", dev, false, &c_host);
     if (rc) return rc;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    // a captured plan copy would replay from a host slot that later calls
+    // overwrite, so the path refuses capture instead of recording it
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    const cudaError_t ce = cudaStreamIsCapturing(stream, &cap);
+    if (ce != cudaSuccess)
+        return nfail(JX_ERR_CUDA, "cudaStreamIsCapturing failed: %s", cudaGetErrorString(ce));
+    if (cap != cudaStreamCaptureStatusNone)
+        return nfail(JX_ERR_UNSUPPORTED,
+                     "jx_attn_step_noalloc cannot be captured into a CUDA graph (its work plan "
+                     "is copied from a host slot that later calls reuse)");
 
     std::lock_guard<std::mutex> lk(g_mu);
     rc = setup_device(dev);

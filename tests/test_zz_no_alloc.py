@@ -256,3 +256,49 @@ def test_noalloc_refuses_pageable_and_host_cache_pointers():
     assert call(dev_in[0].data_ptr(), pageable.ctypes.data) == _lib.JX_ERR_INVALID
     assert b"k_cache" in native.jx_last_error_string()
     torch.cuda.synchronize()
+
+
+def test_noalloc_refuses_stream_capture():
+    # a captured plan copy would replay from a host slot that later calls
+    # reuse, so the call is refused while its stream is capturing
+    import torch
+
+    import jxai_b200 as jx
+    from jxai_b200 import _lib
+    from jxai_b200.attention import _layer_array
+
+    H, HK, hd, L, cap = 8, 2, 64, 1, 64
+    layers = [jx.Layer(hd, hd, 5e5, 0)]
+    desc = _lib.KvDesc(1, L, cap, HK * hd, _lib.JX_F32, 0, 0)
+    arr, keep = _layer_array(layers)
+    cache = torch.zeros(2, cap * HK * hd, device="cuda")
+    io = torch.zeros(4, H * hd, device="cuda")
+    pos = (C.c_int32 * 1)(10)
+    native = jx.load_library()
+    a = _lib.StepArgs()
+    a.n_heads, a.n_kv_heads, a.n_seqs = H, HK, 1
+    a.pos = C.cast(pos, C.POINTER(C.c_int32))
+    a.q, a.k, a.v, a.out = (io[i].data_ptr() for i in range(4))
+    a.q_stride, a.kv_stride = H * hd, HK * hd
+    a.scale, a.yarn_scale, a.rope_neox = 0.125, 1.0, 1
+    # one ordinary call first (the device's set-up), then one under capture
+    s = torch.cuda.Stream()
+    assert native.jx_attn_step_noalloc(C.byref(desc), cache[0].data_ptr(), cache[1].data_ptr(),
+                                       arr, L, C.byref(a), s.cuda_stream) == _lib.JX_OK
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    rc = None
+    with torch.cuda.stream(s):
+        g.capture_begin()
+        try:
+            rc = native.jx_attn_step_noalloc(C.byref(desc), cache[0].data_ptr(),
+                                             cache[1].data_ptr(), arr, L, C.byref(a),
+                                             s.cuda_stream)
+        finally:
+            g.capture_end()
+    assert rc == _lib.JX_ERR_UNSUPPORTED
+    assert b"captured" in native.jx_last_error_string()
+    code = C.c_int(-1)
+    assert native.jx_noalloc_check_device_error(0, C.byref(code), s.cuda_stream) == _lib.JX_OK
+    assert code.value == 0
+    del g
