@@ -257,7 +257,13 @@ JX_API int jx_kv_check_device_error(jx_kv* kv, int* code, void* stream);
  * word and finishes (the step's output is then invalid);
  * "test_wait_cta" N > 0 makes CTA N-1 of every launch wait once on a barrier
  * nothing arrives at -- a test of that error path (use with a short
- * "wait_limit_ms"; 0 = off). */
+ * "wait_limit_ms"; 0 = off); "prefill_tc" 1 (default) / 0 runs prompts on
+ * 16-bit caches on the tensor-core kernel / the decode kernel's token blocks;
+ * "prefill_l2_mb" (default 32) is the L2 budget for the K/V rows the
+ * tensor-core prefill's CTAs read at one time: when a call's K/V rows exceed
+ * L2, its work items go in batches of as many (sequence, layer, kv head)
+ * streams as fit it (0, or rows that fit L2: all items largest first,
+ * strided over the CTAs). */
 JX_API int jx_kv_set_option(jx_kv* kv, const char* key, int value);
 
 /* Device time of the last step recorded with option "timing" (waits for it):

@@ -118,6 +118,7 @@ static_assert(sizeof(PrefillTile) == 64, "PrefillTile layout");
 
 struct PrefillArgs {
     const PrefillTile* tiles;
+    const int* cta_first;  // CTA b runs tiles [cta_first[b], cta_first[b + 1])
     int n_items;
     int neox;
     int q_vec;  // 1: q rows start 16-byte aligned (16-byte loads)

@@ -359,6 +359,7 @@ struct jx_kv {
     CUtensorMap tmKp[2], tmVp[2];
     bool tmp_ok[2] = {false, false};
     int opt_prefill_tc = 1;  // 16-bit caches: prefill attention on the tensor cores (tcgen05)
+    int opt_prefill_l2_mb = 32;  // L2 budget of the K/V streams prefill CTAs share at one time
     std::vector<uint32_t> seq_pos;
     int num_sms = 0;
     int* d_err = nullptr;
@@ -783,9 +784,44 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
             t.rope_half <= hd / 2;
         if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent prefill work item");
     }
-    std::stable_sort(items.begin(), items.end(), [](const PrefillTile& x, const PrefillTile& y) {
-        return x.n_tiles > y.n_tiles;
-    });
+    const int grid = static_cast<int>(std::min<size_t>(std::max(kv->num_sms, 1), items.size()));
+    std::vector<int> cta_first;
+    {
+        std::vector<long long> stream(items.size());
+        std::vector<int> tiles(items.size());
+        for (size_t i = 0; i < items.size(); ++i) {
+            const PrefillTile& t = items[i];
+            stream[i] = (static_cast<long long>(t.seq) * D.n_layers + t.cache_layer) *
+                            static_cast<long long>(a->n_kv_heads) + t.kvh;
+            tiles[i] = t.n_tiles;
+        }
+        // Streams per batch: as many as fit the L2 budget (option
+        // prefill_l2_mb), once all streams' rows together exceed L2 (126 MB);
+        // below that they stay in L2 whatever the order, and striding the
+        // items largest first balances the CTAs best.  Measured (bf16, one
+        // prompt): 2048-token Llama-3.2-1B (67 MB of K/V) strided 1.46 ms,
+        // batched 2.0-2.2; 8192-token Llama-3.2-1B (268 MB) 16.8 / 15.9 ms;
+        // 8192-token Mistral-7B (1.07 GB) 60.4 / 54.3 ms.
+        int window = 0;
+        if (kv->opt_prefill_l2_mb > 0) {
+            std::map<long long, int> stream_tiles;
+            for (size_t i = 0; i < tiles.size(); ++i)
+                stream_tiles[stream[i]] = std::max(stream_tiles[stream[i]], tiles[i]);
+            double all_bytes = 0, max_bytes = 1;
+            for (const auto& st : stream_tiles) {
+                const double b = 2.0 * st.second * BN * hd * 2;  // K and V rows, 16-bit
+                all_bytes += b;
+                max_bytes = std::max(max_bytes, b);
+            }
+            if (all_bytes > 126.0 * 1048576.0)
+                window = static_cast<int>(std::max(
+                    1.0, std::floor(kv->opt_prefill_l2_mb * 1048576.0 / max_bytes)));
+        }
+        const std::vector<size_t> order = schedule_items(stream, tiles, grid, 2, window, cta_first);
+        std::vector<PrefillTile> sorted(items.size());
+        for (size_t i = 0; i < order.size(); ++i) sorted[i] = items[order[i]];
+        items.swap(sorted);
+    }
     for (const PairRow& ap : appends) {
         const bool ok = ap.append_row < 0 ||
                         (ap.append_row >= 0 &&
@@ -796,11 +832,14 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
         if (!ok) return fail(JX_ERR_INVALID, "internal: inconsistent prefill append row");
     }
     const size_t item_bytes = items.size() * sizeof(PrefillTile);
-    const size_t app_off = (item_bytes + 255) & ~static_cast<size_t>(255);
+    const size_t first_off = (item_bytes + 255) & ~static_cast<size_t>(255);
+    const size_t first_bytes = cta_first.size() * sizeof(int);
+    const size_t app_off = (first_off + first_bytes + 255) & ~static_cast<size_t>(255);
     const size_t app_bytes = appends.size() * sizeof(PairRow);
     const size_t rope_off = (app_off + app_bytes + 255) & ~static_cast<size_t>(255);
     std::vector<unsigned char> bytes(rope_off + rope.size() * sizeof(float2), 0);
     std::memcpy(bytes.data(), items.data(), item_bytes);
+    std::memcpy(bytes.data() + first_off, cta_first.data(), first_bytes);
     std::memcpy(bytes.data() + app_off, appends.data(), app_bytes);
     if (!rope.empty()) std::memcpy(bytes.data() + rope_off, rope.data(), rope.size() * sizeof(float2));
     const size_t slot = gi;
@@ -828,6 +867,8 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
     }
     PrefillArgs pa{};
     pa.tiles = static_cast<const PrefillTile*>(kv->slots[slot].d_buf);
+    pa.cta_first = reinterpret_cast<const int*>(static_cast<unsigned char*>(kv->slots[slot].d_buf) +
+                                                first_off);
     pa.n_items = static_cast<int>(items.size());
     pa.neox = neox ? 1 : 0;
     pa.q_vec = (reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride % 4 == 0) ? 1 : 0;
@@ -842,7 +883,6 @@ int prefill_tc(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers,
     pa.err = kv->d_err;
     pa.dbg = kv->d_dbg;
     pa.wait_limit = wait_limit_cycles(kv->opt_wait_limit_ms);
-    const int grid = static_cast<int>(std::min<size_t>(std::max(kv->num_sms, 1), items.size()));
     const cudaError_t e = prefill_tc_launch(pa, &kv->tmKp[kind], &kv->tmVp[kind], hd, D.dtype,
                                             static_cast<int>(G), grid, stream);
     if (e != cudaSuccess)
@@ -1850,6 +1890,10 @@ int jx_kv_set_option(jx_kv* kv, const char* key, int value) {
         kv->opt_split_penalty_us = value < 0 ? -1.0f : static_cast<float>(value);
     else if (!std::strcmp(key, "wait_limit_ms")) kv->opt_wait_limit_ms = value;
     else if (!std::strcmp(key, "prefill_tc")) kv->opt_prefill_tc = value ? 1 : 0;
+    else if (!std::strcmp(key, "prefill_l2_mb")) {
+        if (value < 0) return fail(JX_ERR_INVALID, "prefill_l2_mb must be >= 0");
+        kv->opt_prefill_l2_mb = value;
+    }
     else if (!std::strcmp(key, "test_wait_cta")) kv->opt_test_wait_cta = value;
     else return fail(JX_ERR_INVALID, "unknown option '%s'", key);
     return JX_OK;

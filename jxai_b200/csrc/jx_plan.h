@@ -4,7 +4,12 @@
 #pragma once
 
 #include <algorithm>
+#include <cstddef>
+#include <functional>
+#include <map>
+#include <queue>
 #include <type_traits>
+#include <utility>
 #include <vector>
 
 namespace jx {
@@ -110,6 +115,76 @@ inline std::vector<long long> balanced_split(const std::vector<long long>& seg_o
     }
     pass(hi, true);
     return b;
+}
+
+// Order and CTA assignment of the tensor-core prefill's work items: item i
+// reads the cache rows of K/V stream stream[i] (sequence, cache layer, kv
+// head) in tiles[i] tiles.  Returns the items in launch order, where CTA b of
+// P runs [first[b], first[b + 1]).
+//  * window == 0: all items largest first, CTA b taking items b, b + P, ...
+//    (balanced, but the CTAs working at one time read P different streams).
+//  * window = k > 0: the streams (those with the largest item first) go in
+//    batches of k; each batch's items largest first, batch after batch, so the
+//    CTAs working at one time share about k streams' rows through L2.  The
+//    last 3P items are ordered largest first across batches, so the CTAs end
+//    together.  Items are dealt by list scheduling: each to the CTA whose
+//    earlier items end first, at a cost of its tiles plus item_cost (staging
+//    its queries).
+inline std::vector<size_t> schedule_items(const std::vector<long long>& stream,
+                                          const std::vector<int>& tiles, int P,
+                                          long long item_cost, int window,
+                                          std::vector<int>& first) {
+    const size_t n = tiles.size();
+    const size_t np = static_cast<size_t>(std::max(P, 1));
+    std::vector<size_t> idx(n);
+    for (size_t i = 0; i < n; ++i) idx[i] = i;
+    auto larger = [&](size_t x, size_t y) { return tiles[x] > tiles[y]; };
+    std::vector<std::vector<size_t>> lists(np);
+    if (window <= 0) {
+        std::stable_sort(idx.begin(), idx.end(), larger);
+        for (size_t k = 0; k < n; ++k) lists[k % np].push_back(idx[k]);
+    } else {
+        std::map<long long, int> gid;
+        std::vector<int> g_of(n), gmax;
+        for (size_t i = 0; i < n; ++i) {
+            const auto ins = gid.emplace(stream[i], static_cast<int>(gid.size()));
+            const int g = ins.first->second;
+            if (ins.second) gmax.push_back(0);
+            gmax[static_cast<size_t>(g)] = std::max(gmax[static_cast<size_t>(g)], tiles[i]);
+            g_of[i] = g;
+        }
+        std::vector<int> gorder(gmax.size()), batch(gmax.size());
+        for (size_t g = 0; g < gorder.size(); ++g) gorder[g] = static_cast<int>(g);
+        std::stable_sort(gorder.begin(), gorder.end(), [&](int x, int y) {
+            return gmax[static_cast<size_t>(x)] > gmax[static_cast<size_t>(y)];
+        });
+        for (size_t r = 0; r < gorder.size(); ++r)
+            batch[static_cast<size_t>(gorder[r])] = static_cast<int>(r / static_cast<size_t>(window));
+        std::stable_sort(idx.begin(), idx.end(), [&](size_t x, size_t y) {
+            const int bx = batch[static_cast<size_t>(g_of[x])], by = batch[static_cast<size_t>(g_of[y])];
+            if (bx != by) return bx < by;
+            return tiles[x] > tiles[y];
+        });
+        const size_t tail = std::min(n, 3 * np);
+        std::stable_sort(idx.end() - static_cast<std::ptrdiff_t>(tail), idx.end(), larger);
+        using Slot = std::pair<long long, int>;  // (time this CTA's items end, CTA)
+        std::priority_queue<Slot, std::vector<Slot>, std::greater<Slot>> free_at;
+        for (size_t b = 0; b < np; ++b) free_at.push({0, static_cast<int>(b)});
+        for (size_t i : idx) {
+            const Slot sl = free_at.top();
+            free_at.pop();
+            lists[static_cast<size_t>(sl.second)].push_back(i);
+            free_at.push({sl.first + tiles[i] + item_cost, sl.second});
+        }
+    }
+    std::vector<size_t> order;
+    order.reserve(n);
+    first.assign(np + 1, 0);
+    for (size_t b = 0; b < np; ++b) {
+        for (size_t i : lists[b]) order.push_back(i);
+        first[b + 1] = static_cast<int>(order.size());
+    }
+    return order;
 }
 
 }  // namespace jx

@@ -178,7 +178,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::OFF_MISC + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long wlim = a.wait_limit > 0 ? a.wait_limit : kWaitLimitCycles;
-    const int P = gridDim.x;
+    // this CTA's items: a contiguous run of the plan (the host's schedule)
+    const int it_begin = a.cta_first[blockIdx.x], it_end = a.cta_first[blockIdx.x + 1];
 #define BAR(i) (bars + 8u * static_cast<uint32_t>(i))
 #define WAIT(i, par, site, idx) \
     mbar_wait_bounded(BAR(i), (par), abort_flag, a.err, a.dbg, (site), (idx), true, wlim)
@@ -218,13 +219,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             prefetch_tensormap(&tmV);
         }
         int g = 0, n_issued = 0;
-        for (int it = blockIdx.x; it < a.n_items; it += P) {
+        for (int it = it_begin; it < it_end; ++it) {
             const PrefillTile tl = a.tiles[it];
-            if (it + P < a.n_items) {
+            if (it + 1 < it_end) {
                 // the next item's 128 q rows and their (cos, sin) rows into L2
                 // (this warp is idle most of the time): its Q staging then
                 // reads L2, not DRAM
-                const PrefillTile nx = a.tiles[it + P];
+                const PrefillTile nx = a.tiles[it + 1];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int r = lane * 4 + k, jj = r / G, hh = r % G;
@@ -273,7 +274,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         constexpr uint32_t ID_S = idesc_f16(DT, 128, BN, false);
         constexpr uint32_t ID_PV = idesc_f16(DT, 128, HD, true);
         int g = 0, itc = 0;
-        for (int it = blockIdx.x; it < a.n_items; it += P, ++itc) {
+        for (int it = it_begin; it < it_end; ++it, ++itc) {
             const PrefillTile tl = a.tiles[it];
             const int n = tl.n_tiles;
             WAIT(C::B_QF, itc & 1, 24, itc);  // Q of this item staged
@@ -375,7 +376,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             return buf[(hf ^ 1) * 128 + r];
         };
         int g = 0, itc = 0;
-        for (int it = blockIdx.x; it < a.n_items; it += P, ++itc) {
+        for (int it = it_begin; it < it_end; ++it, ++itc) {
             const PrefillTile tl = a.tiles[it];
             const bool live = j < tl.ntok;
             const int hi_r = live ? tl.tok_row0 + j : -1;
