@@ -67,6 +67,17 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
         : "memory");
 }
 
+// Stores 32 consecutive 32-bit TMEM columns of this thread's lane and waits
+// until the stores are done (before a thread synchronisation hands the
+// columns to the tensor cores).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+        "tcgen05.wait::st.sync.aligned;"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
 
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
@@ -148,17 +159,18 @@ struct PfCfg {
     static constexpr int OFF_P = OFF_Q + 2 * QPART;
     static constexpr int OFF_BAR = OFF_P + 2 * PPART;
     // barriers: kv_full[NS], kv_empty[NS], q_full, q_empty, s_full[2],
-    // s_empty[2], p_full, p_empty, o_full[2], o_empty[2], done
+    // s_empty[2], p_full, p_empty, o_full (each P.V done), o_empty (an item's
+    // O read), done
     static constexpr int B_KVF = 0, B_KVE = NS, B_QF = 2 * NS, B_QE = B_QF + 1, B_SF = B_QF + 2,
                          B_SE = B_SF + 2, B_PF = B_SE + 2, B_PE = B_PF + 1, B_OF = B_PE + 1,
-                         B_OE = B_OF + 2, B_DONE = B_OE + 2, NBARS = B_DONE + 1;
+                         B_OE = B_OF + 1, B_DONE = B_OE + 1, NBARS = B_DONE + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // TMEM base, abort flag
     static constexpr int OFF_XCH = OFF_MISC + 16;         // [2][2][128] floats: row exchanges
     static constexpr int SMEM = OFF_XCH + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
     static constexpr int TMEM_COLS = 512;
     static constexpr int COL_S = 0;        // S buffers: columns [0, 2 BN)
-    static constexpr int COL_O = 2 * BN;   // O tile buffers: [2 BN, 2 BN + 2 HD)
-    static_assert(COL_O + 2 * HD <= TMEM_COLS, "TMEM budget");
+    static constexpr int COL_O = 2 * BN;   // the item's O accumulator: [2 BN, 2 BN + HD)
+    static_assert(COL_O + HD <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -194,9 +206,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int s = 0; s < 2; ++s) {
             mbar_init(BAR(C::B_SF + s), 1);
             mbar_init(BAR(C::B_SE + s), kSoftmaxWarps);
-            mbar_init(BAR(C::B_OF + s), 1);
-            mbar_init(BAR(C::B_OE + s), kSoftmaxWarps);
         }
+        mbar_init(BAR(C::B_OF), 1);
+        mbar_init(BAR(C::B_OE), kSoftmaxWarps);
         mbar_init(BAR(C::B_PF), kSoftmaxWarps);
         mbar_init(BAR(C::B_PE), 1);
         mbar_init(BAR(C::B_DONE), 1);
@@ -308,8 +320,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             for (int t = 0; t < n; ++t, ++g) {
                 if (t + 1 < n) issue_s(g + 1);
                 WAIT(C::B_PF, g & 1, 27, g);  // P(g) staged
-                const int ob = g & 1;
-                if (g >= 2) WAIT(C::B_OE + ob, ((g >> 1) - 1) & 1, 28, g);
+                // the item's first P.V overwrites O: the previous item's O read
+                if (t == 0 && itc > 0) WAIT(C::B_OE, (itc - 1) & 1, 28, itc);
                 tc_fence_after();
                 const int st = g % C::NS;
                 const uint32_t vb = sbase + st * C::STAGE_B + C::TILE_B;
@@ -327,7 +339,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     __syncwarp();
                 }
                 if (lane == 0) {
-                    const uint32_t d = tmem + C::COL_O + ob * HD;
+                    // O += P.V, in TMEM across the item's tiles
+                    const uint32_t d = tmem + C::COL_O;
 #pragma unroll
                     for (int part = 0; part < 2; ++part)
 #pragma unroll
@@ -336,9 +349,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                                                (kb / 4) * C::PSLAB + (kb % 4) * 32,
                                                            16, 1024);
                             const uint64_t bd = sw128_desc(vb + kb * 16 * 128, C::KSLAB, 1024);
-                            tc_mma(d, ad, bd, ID_PV, (part | kb) != 0 ? 1u : 0u);
+                            tc_mma(d, ad, bd, ID_PV, (t | part | kb) != 0 ? 1u : 0u);
                         }
-                    tc_commit(BAR(C::B_OF + ob));
+                    tc_commit(BAR(C::B_OF));
                     tc_commit(BAR(C::B_PE));
                     tc_commit(BAR(C::B_KVE + st));
                 }
@@ -514,27 +527,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(BAR(C::B_QF));
 
-            float m = -INFINITY, l = 0.0f, alpha_pend = 0.0f;
-            float o[HW];
-#pragma unroll
-            for (int d = 0; d < HW; ++d) o[d] = 0.0f;
-            // folds this warp's half of tile gg's O (relative to its running max) into o
-            auto add_o = [&](int gg, float alpha) {
-                const int ob = gg & 1;
-                WAIT(C::B_OF + ob, (gg >> 1) & 1, 31, gg);
-                __syncwarp();  // converged for the .sync.aligned loads
-                tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < HW; c += 32) {
-                    uint32_t t32[32];
-                    tmem_ld32(tmem + lane_addr + C::COL_O + ob * HD + hf * HW + c, t32);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], alpha, __uint_as_float(t32[i]));
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(BAR(C::B_OE + ob));
-            };
+            // Running maximum m (the reference p = exp(s - m) is taken against)
+            // and this half's sum l.  O accumulates in TMEM across the item's
+            // tiles; m moves only when a tile's maximum exceeds it by more
+            // than kLazy (p then stays below e^kLazy = 256, exact in the
+            // fp32 sums), and O and l are rescaled then -- rarely after the
+            // first tiles, so the softmax does not wait for each tile's P.V.
+            constexpr float kLazy = 5.545177444479562f;  // 8 ln 2
+            float m = -INFINITY, l = 0.0f;
             const int n = tl.n_tiles;
             // unscale is a power of two: (S * unscale) * scale rounds once, as
             // the reference's dot * scale does
@@ -582,14 +582,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
                 float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
                 mt = fmaxf(mt, exchange(mt));  // the row's maximum over both halves
-                const float mn = fmaxf(m, mt);
-                const float alpha = m == -INFINITY ? 0.0f : ex2_approx((m - mn) * kLog2eP);
-                m = mn;
+                // both warps of a row see the same mt and m, so they move m together
+                const bool move = mt > m + kLazy || (m == -INFINITY && mt > -INFINITY);
+                if (__any_sync(0xffffffffu, move)) {
+                    const float alpha = (!move || m == -INFINITY) ? (move ? 0.0f : 1.0f)
+                                                                    : ex2_approx((m - mt) * kLog2eP);
+                    if (move) {
+                        l *= alpha;
+                        m = mt;
+                    }
+                    // O holds P.V of tiles [0, t): rescale this half of it once the
+                    // last of those has landed.  A row whose m was -inf has O = 0
+                    // (all its p were 0) and alpha = 0.
+                    if (t > 0) {
+                        WAIT(C::B_OF, (g - 1) & 1, 31, g);
+                        __syncwarp();
+                        tc_fence_after();
+#pragma unroll
+                        for (int c = 0; c < HW; c += 32) {
+                            uint32_t t32[32];
+                            tmem_ld32(tmem + lane_addr + C::COL_O + hf * HW + c, t32);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                t32[i] = __float_as_uint(__uint_as_float(t32[i]) * alpha);
+                            tmem_st32(tmem + lane_addr + C::COL_O + hf * HW + c, t32);
+                        }
+                    }
+                }
                 // p = exp(s - m) and its hi / lo 16-bit parts, in registers before
                 // waiting for the P buffer (this overlaps the previous P.V).
-                // ex2(-inf) is +0, so masked columns need no test once the max is
+                // ex2(-inf) is +0, so masked columns need no test once m is
                 // finite (a row with no attended column yet uses 0).
-                const float mref = mn == -INFINITY ? 0.0f : mn;
+                const float mref = m == -INFINITY ? 0.0f : m;
                 uint32_t hw[SW / 2], lw[SW / 2];
                 float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -613,7 +637,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
                     }
                 }
-                const float ls = (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
+                l += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);  // this half's columns
                 if (g >= 1) WAIT(C::B_PE, (g - 1) & 1, 33, g);  // P.V of the previous tile read P
 #pragma unroll
                 for (int cc = 0; cc < SW / 8; ++cc) {
@@ -626,24 +650,36 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         make_uint4(lw[4 * cc], lw[4 * cc + 1], lw[4 * cc + 2], lw[4 * cc + 3]);
                 }
                 fence_proxy_async_shared();
+                tc_fence_before();  // the O rescale's TMEM stores, before P.V reads O
                 __syncwarp();
                 if (lane == 0) mbar_arrive(BAR(C::B_PF));
-                l = l * alpha + ls;  // this half's columns (alpha is the same in both halves)
-                if (t >= 1) add_o(g - 1, alpha_pend);
-                alpha_pend = alpha;
             }
-            if (n > 0) add_o(g - 1, alpha_pend);
-            // ---- this half of the output row: o / (l of both halves)
+            // ---- this half of the output row: O / (l of both halves), once the
+            // item's last P.V has landed
             const float lt = l + exchange(l);
-            if (live && lt > 0.0f) {
-                const float inv = 1.0f / lt;
+            if (n > 0) {
+                WAIT(C::B_OF, (g - 1) & 1, 34, g);
+                __syncwarp();
+                tc_fence_after();
                 float* dst = a.out + io * a.q_stride + static_cast<long long>(tl.kvh * G + h) * HD +
                              hf * HW;
+                const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
 #pragma unroll
-                for (int d = 0; d < HW; d += 4)
-                    *reinterpret_cast<float4*>(dst + d) =
-                        make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+                for (int c = 0; c < HW; c += 32) {
+                    uint32_t t32[32];
+                    tmem_ld32(tmem + lane_addr + C::COL_O + hf * HW + c, t32);
+                    if (live && lt > 0.0f) {
+#pragma unroll
+                        for (int d = 0; d < 32; d += 4)
+                            *reinterpret_cast<float4*>(dst + c + d) = make_float4(
+                                __uint_as_float(t32[d]) * inv, __uint_as_float(t32[d + 1]) * inv,
+                                __uint_as_float(t32[d + 2]) * inv, __uint_as_float(t32[d + 3]) * inv);
+                    }
+                }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(BAR(C::B_OE));  // O may be overwritten
         }
     }
 #undef WAIT
