@@ -79,6 +79,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
         : "memory");
 }
 
+// As tmem_st32, 16 columns.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n\t"
+        "tcgen05.wait::st.sync.aligned;"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
                  "r"(ncols)
@@ -118,6 +128,20 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] . B[smem]^T: A read from tensor memory (lane = row,
+// each 32-bit column two consecutive 16-bit elements, the even one in the
+// low half), one CTA, fp32 accumulator.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u)
+        : "memory");
+}
+
 // Shared-memory matrix descriptor of a 128-byte-swizzled operand tile (the
 // layout TMA's SWIZZLE_128B writes: 128-byte rows, 16-byte chunk c of row r at
 // chunk c ^ (r % 8), tile base 1024-byte aligned).  lbo / sbo in bytes:
@@ -145,32 +169,32 @@ __device__ __forceinline__ float f4_at(const float4& v, int i) {
 template <int HD>
 struct PfCfg {
     static constexpr int BN = HD == 64 ? 128 : 64;  // cache rows per K/V tile
-    static constexpr int NS = 3;                    // K/V ring stages
+    static constexpr int NS = 4;                    // K/V ring stages
     static constexpr int NSLAB = HD / 64;           // 128-byte slabs of a head row
     static constexpr int KSLAB = BN * 128;          // one slab of a K or V tile
     static constexpr int TILE_B = KSLAB * NSLAB;    // K (or V) tile
     static constexpr int STAGE_B = 2 * TILE_B;
-    static constexpr int QSLAB = 128 * 128;         // 128 rows x 64 elements
-    static constexpr int QPART = QSLAB * NSLAB;     // one 16-bit part of Q
     static constexpr int PSLAB = 128 * 128;
     static constexpr int PNSLAB = BN / 64;
     static constexpr int PPART = PSLAB * PNSLAB;    // one 16-bit part of P
-    static constexpr int OFF_Q = NS * STAGE_B;
-    static constexpr int OFF_P = OFF_Q + 2 * QPART;
+    static constexpr int OFF_P = NS * STAGE_B;
     static constexpr int OFF_BAR = OFF_P + 2 * PPART;
-    // barriers: kv_full[NS], kv_empty[NS], q_full, q_empty, s_full[2],
+    // barriers: kv_full[NS], kv_empty[NS], q_full[2], q_empty[2], s_full[2],
     // s_empty[2], p_full, p_empty, o_full (each P.V done), o_empty (an item's
     // O read), done
-    static constexpr int B_KVF = 0, B_KVE = NS, B_QF = 2 * NS, B_QE = B_QF + 1, B_SF = B_QF + 2,
+    static constexpr int B_KVF = 0, B_KVE = NS, B_QF = 2 * NS, B_QE = B_QF + 2, B_SF = B_QE + 2,
                          B_SE = B_SF + 2, B_PF = B_SE + 2, B_PE = B_PF + 1, B_OF = B_PE + 1,
                          B_OE = B_OF + 1, B_DONE = B_OE + 1, NBARS = B_DONE + 1;
     static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;  // TMEM base, abort flag
-    static constexpr int OFF_XCH = OFF_MISC + 16;         // [2][2][128] floats: row exchanges
+    static constexpr int OFF_XCH = OFF_MISC + 32;         // [2][2][128] floats: row exchanges
     static constexpr int SMEM = OFF_XCH + 2 * 2 * 128 * 4 + 1024;  // + alignment slack
     static constexpr int TMEM_COLS = 512;
     static constexpr int COL_S = 0;        // S buffers: columns [0, 2 BN)
     static constexpr int COL_O = 2 * BN;   // the item's O accumulator: [2 BN, 2 BN + HD)
-    static_assert(COL_O + HD <= TMEM_COLS, "TMEM budget");
+    // Q of two items (the next one staged while the current one finishes):
+    // buffer b at [COL_Q + b HD, +HD), its hi part in the first HD/2 columns
+    static constexpr int COL_Q = 2 * BN + HD;
+    static_assert(COL_Q + 2 * HD <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -183,7 +207,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     static_assert(128 % G == 0 && G <= 8, "query group");
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    const uint32_t sbase = (raw + 1023u) & ~1023u;  // 128-byte-swizzled tiles: 1024-byte aligned
     unsigned char* base = smem_raw + (sbase - raw);
     const uint32_t bars = sbase + C::OFF_BAR;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::OFF_MISC);
@@ -201,8 +225,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(BAR(C::B_KVF + s), 1);
             mbar_init(BAR(C::B_KVE + s), 1);
         }
-        mbar_init(BAR(C::B_QF), kSoftmaxWarps);
-        mbar_init(BAR(C::B_QE), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(BAR(C::B_QF + b), kSoftmaxWarps);
+            mbar_init(BAR(C::B_QE + b), 1);
+        }
         for (int s = 0; s < 2; ++s) {
             mbar_init(BAR(C::B_SF + s), 1);
             mbar_init(BAR(C::B_SE + s), kSoftmaxWarps);
@@ -289,8 +315,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int it = it_begin; it < it_end; ++it, ++itc) {
             const PrefillTile tl = a.tiles[it];
             const int n = tl.n_tiles;
-            WAIT(C::B_QF, itc & 1, 24, itc);  // Q of this item staged
+            const int qb = itc & 1;
+            WAIT(C::B_QF + qb, (itc >> 1) & 1, 24, itc);  // Q of this item staged
             tc_fence_after();
+            const uint32_t qa = tmem + C::COL_Q + qb * HD;
             // S = Q_hi.K^T + Q_lo.K^T for global tile gg
             auto issue_s = [&](int gg) {
                 const int st = gg % C::NS;
@@ -305,12 +333,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     for (int part = 0; part < 2; ++part)
 #pragma unroll
                         for (int ks = 0; ks < HD / 16; ++ks) {
-                            const uint64_t ad = sw128_desc(sbase + C::OFF_Q + part * C::QPART +
-                                                               (ks / 4) * C::QSLAB + (ks % 4) * 32,
-                                                           16, 1024);
                             const uint64_t bd =
                                 sw128_desc(kb + (ks / 4) * C::KSLAB + (ks % 4) * 32, 16, 1024);
-                            tc_mma(d, ad, bd, ID_S, (part | ks) != 0 ? 1u : 0u);
+                            tc_mma_ts(d, qa + part * (HD / 2) + ks * 8, bd, ID_S,
+                                      (part | ks) != 0 ? 1u : 0u);
                         }
                     tc_commit(BAR(C::B_SF + sb));
                 }
@@ -357,7 +383,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
                 __syncwarp();
             }
-            if (lane == 0) tc_commit(BAR(C::B_QE));  // this item's Q is no longer read
+            if (lane == 0) tc_commit(BAR(C::B_QE + qb));  // this item's Q is no longer read
             __syncwarp();
         }
         // every MMA this thread issued completes before TMEM is freed
@@ -388,15 +414,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             named_bar_sync(1 + q4, 64);
             return buf[(hf ^ 1) * 128 + r];
         };
-        int g = 0, itc = 0;
-        for (int it = it_begin; it < it_end; ++it, ++itc) {
-            const PrefillTile tl = a.tiles[it];
+        // Rotates this warp's half of item tl's query rows, splits them into
+        // hi / lo 16-bit parts and stores them to TMEM Q buffer qi % 2 (the MMA
+        // warp's A operand); returns the power of two S is to be scaled back by.
+        auto stage_q = [&](const PrefillTile& tl, int qi) -> float {
+            const int qb = qi & 1;
             const bool live = j < tl.ntok;
-            const int hi_r = live ? tl.tok_row0 + j : -1;
-            const int lo_r = live ? (tl.window > 0 ? max(tl.row0, hi_r - tl.window + 1) : tl.row0) : 0;
             const long long io = static_cast<long long>(tl.io0) + static_cast<long long>(j) * tl.io_step;
-            // ---- Q: rotate this warp's half of the row, split into hi / lo, stage
-            if (itc > 0) WAIT(C::B_QE, (itc - 1) & 1, 30, itc);
+            if (qi >= 2) WAIT(C::B_QE + qb, ((qi >> 1) - 1) & 1, 30, qi);
             float unscale = 1.0f;
             {
                 // rotation of this warp's half of the row (dims [hf*HW, +HW)),
@@ -509,23 +534,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     up = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
                     unscale = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
                 }
+                // this half's dims [hf*HW, +HW) are columns [hf*HW/2, +HW/2) of
+                // each part (two elements per column, the even one low)
+                uint32_t hw[HW / 2], lw[HW / 2];
 #pragma unroll
-                for (int cc = 0; cc < HW / 8; ++cc) {
-                    const int c = hf * (HW / 8) + cc;  // 16-byte chunk of the row
-                    uint32_t hw4[4], lw4[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        split_pair<DT>(qr[8 * cc + 2 * i] * up, qr[8 * cc + 2 * i + 1] * up, hw4[i],
-                                       lw4[i]);
-                    const int off = C::OFF_Q + (c / 8) * C::QSLAB + r * 128 + (((c % 8) ^ (r & 7)) * 16);
-                    *reinterpret_cast<uint4*>(base + off) = make_uint4(hw4[0], hw4[1], hw4[2], hw4[3]);
-                    *reinterpret_cast<uint4*>(base + off + C::QPART) =
-                        make_uint4(lw4[0], lw4[1], lw4[2], lw4[3]);
+                for (int i = 0; i < HW / 2; ++i)
+                    split_pair<DT>(qr[2 * i] * up, qr[2 * i + 1] * up, hw[i], lw[i]);
+                __syncwarp();  // converged for the .sync.aligned stores
+                const uint32_t qc = tmem + lane_addr + C::COL_Q + qb * HD + hf * (HW / 2);
+                if constexpr (HW / 2 == 16) {
+                    tmem_st16(qc, hw);
+                    tmem_st16(qc + HD / 2, lw);
+                } else {
+                    tmem_st32(qc, hw);
+                    tmem_st32(qc + HD / 2, lw);
                 }
             }
-            fence_proxy_async_shared();  // generic writes -> tensor-core reads
+            tc_fence_before();  // TMEM stores done (wait::st) -> the MMA warp
             __syncwarp();
-            if (lane == 0) mbar_arrive(BAR(C::B_QF));
+            if (lane == 0) mbar_arrive(BAR(C::B_QF + qb));
+            return unscale;
+        };
+        int g = 0, itc = 0;
+        float unscale = it_begin < it_end ? stage_q(a.tiles[it_begin], 0) : 1.0f;
+        for (int it = it_begin; it < it_end; ++it, ++itc) {
+            const PrefillTile tl = a.tiles[it];
+            const bool live = j < tl.ntok;
+            const int hi_r = live ? tl.tok_row0 + j : -1;
+            const int lo_r = live ? (tl.window > 0 ? max(tl.row0, hi_r - tl.window + 1) : tl.row0) : 0;
+            const long long io = static_cast<long long>(tl.io0) + static_cast<long long>(j) * tl.io_step;
 
             // Running maximum m (the reference p = exp(s - m) is taken against)
             // and this half's sum l.  O accumulates in TMEM across the item's
@@ -654,6 +691,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(BAR(C::B_PF));
             }
+            // the next item's Q, while this item's last P.V runs (the MMA warp
+            // can start the next item's S as soon as it is staged)
+            const float unscale_next = it + 1 < it_end ? stage_q(a.tiles[it + 1], itc + 1) : 1.0f;
             // ---- this half of the output row: O / (l of both halves), once the
             // item's last P.V has landed
             const float lt = l + exchange(l);
@@ -680,6 +720,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(BAR(C::B_OE));  // O may be overwritten
+            unscale = unscale_next;
         }
     }
 #undef WAIT
