@@ -68,7 +68,9 @@ def parse_args():
                    help="timed steps (default: 2000 for c1/c2, 200 for the larger configs)")
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--config", default="c4")
+    p.add_argument("--config", default=None,
+                   help="workload c1..c5 (default: c4 for decode steps; c2, the shape the\n"
+                        "reference's prompt loop is measured on, for --prefill / --engine)")
     p.add_argument("--dtype", default=None, help="KV cache type (f32 | bf16 | f16)")
     p.add_argument("--cpu-sample-s", type=float, default=8.0,
                    help="seconds of CPU work for the cpu_baseline sample")
@@ -98,6 +100,8 @@ def parse_args():
                    help="prompt throughput: one prompt of N tokens per jx_attn_prefill call\n"
                         "(full-attention configs), the reference's token-serial loop beside it")
     a = p.parse_args()
+    if a.config is None:
+        a.config = "c2" if (a.prefill or a.engine) else "c4"
     if a.steps is None:
         a.steps = 2000 if a.config.lower() in ("c1", "c2", "qwen2.5-0.5b", "llama-3.2-1b") else 200
     return a
