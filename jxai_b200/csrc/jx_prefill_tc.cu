@@ -11,16 +11,17 @@
 //  * Work item = (run of consecutive prompt tokens of one sequence, layer,
 //    kv head): TQ = 128/G tokens x the G query heads of that kv head are the
 //    M = 128 rows of the MMAs (row r = token r/G, head r%G).
-//  * Warp 0 streams K and V tiles of BN cache rows (BN = 128 at head_dim 64,
-//    64 at head_dim 128) into a 3-stage ring with TMA (128-byte swizzle, no
+//  * Warp 0 streams K and V tiles of 128 cache rows into a ring (4 stages at
+//    head_dim 64, 2 at head_dim 128) with TMA (128-byte swizzle, no
 //    multicast).  Warp 1 owns the tensor memory (512 columns) and issues the
-//    MMAs from one thread: S = Q.K^T into one of two TMEM buffers, then
-//    O_t = P.V into one of two others.  Warps 2-9 (two per TMEM lane quarter,
-//    each with half of a row's columns; one thread per query row = TMEM lane)
-//    rotate and stage Q, read S with tcgen05.ld, apply the scale, soft-cap
-//    and each row's causal / window limits, run the online softmax (row
-//    maxima exchanged between the two halves), stage P, and fold each tile's
-//    O_t into registers with the rescale.
+//    MMAs from one thread: S = Q.K^T into one of two TMEM buffers (Q read
+//    from TMEM), then O += P.V into the item's TMEM accumulator.  Warps 2-9
+//    (two per TMEM lane quarter, each with half of a row's columns; one
+//    thread per query row = TMEM lane) rotate and stage Q into TMEM, read S
+//    with tcgen05.ld, apply the scale, soft-cap and each row's causal /
+//    window limits, run the online softmax (row maxima exchanged between the
+//    two halves; the running maximum moves lazily, O rescaled in TMEM when
+//    it does), stage P, and write each item's O / l.
 //  * Precision.  q and p are fp32; each is split into two 16-bit parts
 //    (hi = rn(x), lo = rn(x - hi)) and both parts are multiplied into the same
 //    fp32 accumulator, while cache values are exact in the operand type -- the
@@ -168,8 +169,12 @@ __device__ __forceinline__ float f4_at(const float4& v, int i) {
 
 template <int HD>
 struct PfCfg {
-    static constexpr int BN = HD == 64 ? 128 : 64;  // cache rows per K/V tile
-    static constexpr int NS = 4;                    // K/V ring stages
+    static constexpr int BN = 128;                  // cache rows per K/V tile
+    // K/V ring stages: 32 KB (head_dim 64) or 64 KB (128) each
+    static constexpr int NS = HD == 64 ? 4 : 2;
+    // Q buffers in TMEM: two (the next item's Q staged while the current
+    // item's S MMAs still read theirs) where the columns allow
+    static constexpr int QBUF = HD == 64 ? 2 : 1;
     static constexpr int NSLAB = HD / 64;           // 128-byte slabs of a head row
     static constexpr int KSLAB = BN * 128;          // one slab of a K or V tile
     static constexpr int TILE_B = KSLAB * NSLAB;    // K (or V) tile
@@ -191,10 +196,10 @@ struct PfCfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int COL_S = 0;        // S buffers: columns [0, 2 BN)
     static constexpr int COL_O = 2 * BN;   // the item's O accumulator: [2 BN, 2 BN + HD)
-    // Q of two items (the next one staged while the current one finishes):
-    // buffer b at [COL_Q + b HD, +HD), its hi part in the first HD/2 columns
+    // Q of QBUF items: buffer b at [COL_Q + b HD, +HD), its hi part in the
+    // first HD/2 columns
     static constexpr int COL_Q = 2 * BN + HD;
-    static_assert(COL_Q + 2 * HD <= TMEM_COLS, "TMEM budget");
+    static_assert(COL_Q + QBUF * HD <= TMEM_COLS, "TMEM budget");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -315,8 +320,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int it = it_begin; it < it_end; ++it, ++itc) {
             const PrefillTile tl = a.tiles[it];
             const int n = tl.n_tiles;
-            const int qb = itc & 1;
-            WAIT(C::B_QF + qb, (itc >> 1) & 1, 24, itc);  // Q of this item staged
+            const int qb = itc % C::QBUF;
+            WAIT(C::B_QF + qb, (itc / C::QBUF) & 1, 24, itc);  // Q of this item staged
             tc_fence_after();
             const uint32_t qa = tmem + C::COL_Q + qb * HD;
             // S = Q_hi.K^T + Q_lo.K^T for global tile gg
@@ -415,13 +420,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             return buf[(hf ^ 1) * 128 + r];
         };
         // Rotates this warp's half of item tl's query rows, splits them into
-        // hi / lo 16-bit parts and stores them to TMEM Q buffer qi % 2 (the MMA
+        // hi / lo 16-bit parts and stores them to TMEM Q buffer qi % QBUF (the MMA
         // warp's A operand); returns the power of two S is to be scaled back by.
         auto stage_q = [&](const PrefillTile& tl, int qi) -> float {
-            const int qb = qi & 1;
+            const int qb = qi % C::QBUF;
             const bool live = j < tl.ntok;
             const long long io = static_cast<long long>(tl.io0) + static_cast<long long>(j) * tl.io_step;
-            if (qi >= 2) WAIT(C::B_QE + qb, ((qi >> 1) - 1) & 1, 30, qi);
+            if (qi >= C::QBUF) WAIT(C::B_QE + qb, ((qi / C::QBUF) - 1) & 1, 30, qi);
             float unscale = 1.0f;
             {
                 // rotation of this warp's half of the row (dims [hf*HW, +HW)),

@@ -2,8 +2,8 @@
 
 jx_attn_prefill on a bf16 or fp16-truncated cache with head_dim 64/128 and a
 query group of 1, 2, 4 or 8 runs the prompt's attention on the tensor cores:
-128/G tokens x G heads per tile, K/V tiles of 128 (head_dim 64) or 64
-(head_dim 128) cache rows, q and p split into two 16-bit parts.  Every case
+128/G tokens x G heads per tile, K/V tiles of 128 cache rows, q and p split
+into two 16-bit parts.  Every case
 here is checked against the reference's own loop run one token at a time
 (src/transformer.cpp:3092-3095, the block of :2497-2566): outputs within
 1e-4, cache bytes identical.  The prompts are long enough for many query
@@ -145,3 +145,51 @@ def test_tc_prefill_agrees_with_cuda_core_path(dtype):
                    options={"prefill_tc": 0})
     assert np.abs(a - b).max() <= TOL
     assert n_tc == n_cc == 1  # one attention launch per head_dim group either way
+
+
+def test_tc_prefill_schedules_agree_beyond_l2():
+    # A prompt whose K/V rows (134 MB) exceed L2 is scheduled in batches of
+    # (sequence, layer, kv head) streams; with option prefill_l2_mb = 0 the
+    # same items run strided, largest first.  Each item's arithmetic does not
+    # depend on which CTA runs it, so the outputs must agree bit for bit; the
+    # last tokens of one layer are also checked against the oracle.
+    import torch
+    import jxai_b200 as jx
+    from oracle.oracle import BF16
+    N, L, H, HK, HD = 4096, 8, 32, 8, 128
+    rs = HK * HD
+    layers = [jx.Layer(HD, HD, 5e5, l) for l in range(L)]
+    q = torch.empty(N, L, H * HD, device="cuda")
+    k = torch.empty(N, L, rs, device="cuda")
+    v = torch.empty_like(k)
+    jx.fill_normal(q, 11, 1)
+    jx.fill_normal(k, 11, 2)
+    jx.fill_normal(v, 11, 3)
+    outs = []
+    for mb in (None, 0):
+        cache = jx.KVCache(1, L, N, rs, BF16)
+        try:
+            if mb is not None:
+                cache.set_option("prefill_l2_mb", mb)
+            out = torch.full_like(q, float("nan"))
+            jx.attn_prefill(cache, layers, q, k, v, out, list(range(N)), H, HK, neox=True)
+            torch.cuda.synchronize()
+            assert cache.check_device_error() == 0
+            outs.append(out)
+            if mb is None:
+                kc = cache.read_rows(0, 3, 0, 0, N)
+                vc = cache.read_rows(0, 3, 1, 0, N)
+        finally:
+            cache.close()
+    assert torch.equal(outs[0], outs[1])
+    # oracle on the last 3 tokens of layer 3 (cache rows as stored)
+    from tests.helpers import oracle_step
+    got = outs[0].cpu().numpy()
+    qh, kh, vh = q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy()
+    lay = [jx.Layer(HD, HD, 5e5, 0)]  # layer 3's rope, on the one-layer host copy
+    for t in (N - 3, N - 2, N - 1):
+        ko = kc[None, None].copy()
+        vo = vc[None, None].copy()
+        ref = oracle_step(ko, vo, BF16, [t], lay, qh[t:t + 1, 3:4], kh[t:t + 1, 3:4],
+                          vh[t:t + 1, 3:4], H, HK, HD, 1 / math.sqrt(HD), neox=True)[0]
+        assert np.abs(got[t, 3] - ref[0]).max() <= TOL
