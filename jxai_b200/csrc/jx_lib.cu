@@ -507,14 +507,27 @@ int upload_plan(jx_kv* kv, size_t slot_i, const std::vector<unsigned char>& byte
         JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
                                 stream));
     } else {
-        if (!kv->up_stream)
-            JX_CUDA(cudaStreamCreateWithFlags(&kv->up_stream, cudaStreamNonBlocking));
-        if (s.used_pending[b]) JX_CUDA(cudaStreamWaitEvent(kv->up_stream, s.ev_used[b], 0));
-        JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
-                                kv->up_stream));
-        JX_CUDA(cudaEventRecord(s.ev_copy[b], kv->up_stream));
+        const cudaError_t busy = cudaStreamQuery(stream);
+        if (busy == cudaErrorNotReady && cudaPeekAtLastError() == cudaErrorNotReady)
+            cudaGetLastError();  // a status, not an error of the caller's
+        if (busy == cudaSuccess) {
+            // nothing queued on the stream (a caller that synchronises every
+            // call): copy in it, with no cross-stream wait before the launch
+            JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
+                                    stream));
+            JX_CUDA(cudaEventRecord(s.ev_copy[b], stream));
+        } else {
+            // work in flight: copy on the side stream once the launches that
+            // last read this buffer have run, so the copy overlaps that work
+            if (!kv->up_stream)
+                JX_CUDA(cudaStreamCreateWithFlags(&kv->up_stream, cudaStreamNonBlocking));
+            if (s.used_pending[b]) JX_CUDA(cudaStreamWaitEvent(kv->up_stream, s.ev_used[b], 0));
+            JX_CUDA(cudaMemcpyAsync(s.d_ring[b], s.h_buf[b], bytes.size(), cudaMemcpyHostToDevice,
+                                    kv->up_stream));
+            JX_CUDA(cudaEventRecord(s.ev_copy[b], kv->up_stream));
+            JX_CUDA(cudaStreamWaitEvent(stream, s.ev_copy[b], 0));
+        }
         s.copy_pending[b] = true;
-        JX_CUDA(cudaStreamWaitEvent(stream, s.ev_copy[b], 0));
     }
     s.d_buf = s.d_ring[b];
     s.cur = b;
