@@ -316,7 +316,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     w = make_workload(args)
     # the end-to-end leg decodes warmup + K further tokens: room for their rows
-    extra = 0 if args.no_e2e else args.warmup + args.steps
+    extra = 0 if args.no_e2e else args.warmup + args.steps + 16
     r = Runner(w, rank, world, local_rank, args.set, extra_rows=extra)
     stream = torch.cuda.current_stream()
 
@@ -521,6 +521,23 @@ def run_ours(args, rank, world, local_rank):
         if r.cache.check_device_error():
             raise RuntimeError("device error during the end-to-end steps")
         e2e_ms = max_over_ranks(a.elapsed_time(b))
+        # The host's own cost of a call, without back-pressure: in the loop
+        # above the host runs ahead until the library's plan copies (four in
+        # flight) wait for the GPU, so host_issue equals the step whenever the
+        # GPU is the slower side.  Here: bursts of three calls, each burst
+        # issued on an idle GPU, median over five bursts.
+        bursts = []
+        i0 = args.warmup + K
+        for bi in range(5):
+            torch.cuda.synchronize()
+            barrier()
+            h1 = time.perf_counter()
+            for jj in range(3):
+                e2e_step(i0 + 3 * bi + jj)
+            bursts.append((time.perf_counter() - h1) * 1e3 / 3)
+        torch.cuda.synchronize()
+        barrier()
+        host_call_ms = max_over_ranks(statistics.median(bursts))
         e2e_kv = sum_over_ranks(sum(r.kv_bytes_at(i) for i in range(args.warmup,
                                                                      args.warmup + K)))
         h2d = sum_over_ranks((qh.numel() + kh.numel() + vh.numel()) * 4)
@@ -529,6 +546,7 @@ def run_ours(args, rank, world, local_rank):
                "ms_per_step": round(e2e_ms / K, 5), "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h),
                "host_issue_ms_per_step": round(host_ms, 5),
+               "host_call_ms": round(host_call_ms, 5),
                "positions": f"advancing: step i appends row T-1+i and attends T+i rows "
                             f"(i = {args.warmup}..{args.warmup + K - 1} timed)",
                "path": ("pinned host q|k|v and attn_out passed to jx_attn_step (C ABI); the "
