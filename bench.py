@@ -141,7 +141,8 @@ def tensor_peak():
 
 
 def ncu_traffic(key: str):
-    """DRAM bytes per launch of the decode kernel from the committed ncu summary."""
+    """DRAM bytes per launch of a kernel from the committed ncu summaries (the
+    decode kernel per workload, the tensor-core prefill per prompt)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(path) as fh:
@@ -854,7 +855,8 @@ def run_prefill(args, rank, world):
         achieved = flops / (ms * 1e-3) / 1e12
         peak, src = tensor_peak()
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
-                "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+                "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                "traffic": ncu_traffic(f"prefill/{w.name}/{w.dtype}/{N}"),
                 "kernel": "jx::prefill_tc_kernel", "kernel_ms": round(ms, 4),
                 "alg_flops_per_call": flops,
                 "issued_tflops": round(2 * achieved, 2),
