@@ -381,6 +381,8 @@ struct jx_kv {
     int last_launches = 0;
     // launch shape per (head_dim, group, stages override): {stages, ctas per SM}
     std::map<std::tuple<int, int, int, int>, std::pair<int, int>> shapes;
+    // per (segments + 1, CTAs): the slice budget of the last plan (warm start)
+    std::map<std::pair<long long, long long>, long long> split_hints;
     // Replay of the last step: a call identical to the previous one (same
     // arguments, positions, layers, buffers, stream, options) relaunches the
     // launches built for it, as long as no plan buffer or scratch changed since.
@@ -1211,7 +1213,10 @@ int step_impl(jx_kv* kv, const jx_layer_desc* layers, uint32_t n_layers, const j
                 for (uint32_t h = 0; h < n_kv; ++h)
                     if (pr.len > 0) seg_off.push_back(pr.off + static_cast<long long>(h) * pr.len);
             seg_off.push_back(total);
-            cta_begin = balanced_split(seg_off, total, P, penalty_rows);
+            // the previous call's budget for this layout size as a warm start
+            if (kv->split_hints.size() > 64) kv->split_hints.clear();
+            long long& hint = kv->split_hints[std::make_pair(static_cast<long long>(seg_off.size()), P)];
+            cta_begin = balanced_split(seg_off, total, P, penalty_rows, -1, &hint);
             seg_owner.assign(static_cast<size_t>(n_kv_segs) * 2, 0);
             size_t c = 0;
             long long si = 0;

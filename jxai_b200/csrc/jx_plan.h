@@ -18,8 +18,11 @@ namespace jx {
 // seg_off[j], seg_off.back() == total) so that every CTA's rows plus
 // `penalty` rows per extra piece (each segment boundary inside its slice)
 // come out equal.
-//  * Few segments per CTA: the smallest per-CTA budget that covers every row,
-//    by bisection (each step a walk over the CTAs and segments).
+//  * Few segments per CTA: the smallest whole-row per-CTA budget that covers
+//    every row, by bisection (each step a walk over the CTAs and segments).
+//    *hint (optional) is the budget of a previous call, updated on return:
+//    a decode loop's next step moves it by about one row, so the search
+//    brackets it in a few passes -- with the same result as without a hint.
 //  * Many (a prefill's thousands of short segments): one pass -- with
 //    F(x) = x + penalty * (segment starts <= x), CTA c takes
 //    [F^-1(c*C/P), F^-1((c+1)*C/P)), C = F(total).  Here a CTA's share is
@@ -27,7 +30,7 @@ namespace jx {
 //    (which would leave it empty).
 inline std::vector<long long> balanced_split(const std::vector<long long>& seg_off,
                                              long long total, long long P, double penalty,
-                                             int form = -1) {
+                                             int form = -1, long long* hint = nullptr) {
     std::vector<long long> b(static_cast<size_t>(P) + 1, total);
     const size_t m = seg_off.size() - 1;  // segments
     b[0] = 0;
@@ -107,13 +110,39 @@ inline std::vector<long long> balanced_split(const std::vector<long long>& seg_o
         return long_segments ? layout(budget_rows, write, std::true_type{})
                              : layout(budget_rows, write, std::false_type{});
     };
-    double lo = static_cast<double>(total) / static_cast<double>(P);
-    double hi = lo + penalty * static_cast<double>(m) + 1.0;
-    for (int it = 0; it < 60 && hi - lo > 0.5; ++it) {
-        const double mid = 0.5 * (lo + hi);
-        if (pass(mid, false) >= total) hi = mid; else lo = mid;
+    // lo: below the mean share, so no layout covers the rows; hi: covers them
+    auto covers = [&](long long budget) { return pass(static_cast<double>(budget), false) >= total; };
+    long long lo = std::max<long long>(0, total / P - 1);
+    long long hi = static_cast<long long>(static_cast<double>(total) / static_cast<double>(P) +
+                                          penalty * static_cast<double>(m)) + 2;
+    if (hint && *hint > lo && *hint < hi) {
+        const long long h = *hint;
+        if (covers(h)) {
+            hi = h;
+            for (long long d = 1; h - d > lo; d *= 2) {
+                if (!covers(h - d)) {
+                    lo = h - d;
+                    break;
+                }
+                hi = h - d;
+            }
+        } else {
+            lo = h;
+            for (long long d = 1; h + d < hi; d *= 2) {
+                if (covers(h + d)) {
+                    hi = h + d;
+                    break;
+                }
+                lo = h + d;
+            }
+        }
     }
-    pass(hi, true);
+    while (hi - lo > 1) {
+        const long long mid = lo + (hi - lo) / 2;
+        if (covers(mid)) hi = mid; else lo = mid;
+    }
+    if (hint) *hint = hi;
+    pass(static_cast<double>(hi), true);
     return b;
 }
 

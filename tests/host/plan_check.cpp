@@ -4,7 +4,8 @@
 // CTA, empty segments, small and large per-piece penalties -- it checks that
 // the boundaries start at 0, end at the total and never decrease, and that
 // the bisection's two layout forms (a plain walk over the CTAs, and one that
-// lays out runs of CTAs inside a segment at once) give the same boundaries.
+// lays out runs of CTAs inside a segment at once) give the same boundaries,
+// with or without a warm-start hint.
 // It also checks jx::schedule_items, the order and CTA assignment of the
 // tensor-core prefill's work items: the result is a permutation, the CTA
 // ranges tile it, and no CTA's cost exceeds total / P + the largest item
@@ -41,6 +42,12 @@ int main(int argc, char** argv) {
         if (ok && static_cast<size_t>(m) <= static_cast<size_t>(64 * P)) {
             ok = jx::balanced_split(seg_off, total, P, penalty, 0) == b &&
                  jx::balanced_split(seg_off, total, P, penalty, 1) == b;
+            // a warm-start hint (near or far from the answer) changes nothing
+            long long h = 1 + static_cast<long long>(rng() % (2 * (total / P + 2)));
+            long long h2 = h;
+            ok = ok && jx::balanced_split(seg_off, total, P, penalty, -1, &h) == b;
+            ok = ok && jx::balanced_split(seg_off, total, P, penalty, -1, &h) == b &&
+                 jx::balanced_split(seg_off, total, P, penalty, -1, &h2) == b;
         }
         if (!ok) {
             std::printf("case %d: m=%d P=%lld total=%lld penalty=%f\n", it, m, P, total, penalty);
