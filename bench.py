@@ -191,7 +191,7 @@ class ClockSampler:
             if self.t:
                 self.t.join(timeout=2)
 
-    def summary(self, t0: float, t1: float):
+    def summary(self, t0: float, t1: float, min_samples: int = 1):
         rows = []
         for ts, ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
@@ -203,16 +203,27 @@ class ClockSampler:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        window = [r for r in rows if t0 <= r[0] <= t1] or rows[-5:]
+        window = [r for r in rows if t0 <= r[0] <= t1]
+        extended = False
+        if len(window) < min_samples:
+            # a timed region shorter than a few sample periods: the samples
+            # from its start on (the same steps go on repeating after it)
+            later = [r for r in rows if r[0] >= t0][:min_samples]
+            if len(later) > len(window):
+                window, extended = later, True
+        window = window or rows[-5:]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
         for r in window:
             for nm, v in zip(names, r[3][1:]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
-        return {"sm_mhz": statistics.median(r[1] for r in window),
-                "sm_max_mhz": max(r[2] for r in window), "reasons": sorted(reasons),
-                "samples": len(window)}
+        out = {"sm_mhz": statistics.median(r[1] for r in window),
+               "sm_max_mhz": max(r[2] for r in window), "reasons": sorted(reasons),
+               "samples": len(window)}
+        if extended:
+            out["window"] = "from the timed region's start into the repeats that follow it"
+        return out
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -419,7 +430,6 @@ def run_ours(args, rank, world, local_rank):
         raise RuntimeError(f"device error {err} during the timed region")
     elapsed_ms = max_over_ranks(elapsed_ms)
     total_kv = sum_over_ranks(r.kv_bytes)
-    clocks = sampler.summary(t_wall0, t_wall1)
 
     # ---- sustained: the same K steps repeated for about --sustained-s seconds
     # (a short burst runs at boost clocks; a long one meets the power cap).
@@ -457,6 +467,9 @@ def run_ours(args, rank, world, local_rank):
                      "clocks": sampler.summary(s_wall0, s_wall1)}
     if use_graph:
         del graph
+    # the timed region's clocks; when it spans under 5 samples (100 ms
+    # each), the samples from its start into the sustained repeats after it
+    clocks = sampler.summary(t_wall0, t_wall1, min_samples=5)
     sampler.stop()
 
     # ---- end to end through the public API with host buffers, decoding on:

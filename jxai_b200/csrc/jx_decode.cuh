@@ -1034,9 +1034,10 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
             // ---- scores: lane = row
             float s[GS];
             if (lane < nvalid) {
-                float acc[GS];
+                // even and odd dims summed apart, two per fp32x2 FMA, then added
+                float acc[GS], acc1[GS];
 #pragma unroll
-                for (int g = 0; g < GS; ++g) acc[g] = 0.0f;
+                for (int g = 0; g < GS; ++g) acc[g] = acc1[g] = 0.0f;
 #pragma unroll 4
                 for (int j = 0; j < G::CHUNKS; ++j) {
                     const uint4 raw = *reinterpret_cast<const uint4*>(
@@ -1049,13 +1050,13 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                         for (int g = 0; g < GS; ++g) {
                             const float4 qv =
                                 *reinterpret_cast<const float4*>(q_s + g * HD + j * G::EPC + e4);
-                            acc[g] = __fmaf_rn(qv.x, kv[e4 + 0], acc[g]);
-                            acc[g] = __fmaf_rn(qv.y, kv[e4 + 1], acc[g]);
-                            acc[g] = __fmaf_rn(qv.z, kv[e4 + 2], acc[g]);
-                            acc[g] = __fmaf_rn(qv.w, kv[e4 + 3], acc[g]);
+                            fma_x2(acc[g], acc1[g], qv.x, qv.y, kv[e4 + 0], kv[e4 + 1]);
+                            fma_x2(acc[g], acc1[g], qv.z, qv.w, kv[e4 + 2], kv[e4 + 3]);
                         }
                     }
                 }
+#pragma unroll
+                for (int g = 0; g < GS; ++g) acc[g] = __fadd_rn(acc[g], acc1[g]);
 #pragma unroll
                 for (int g = 0; g < GS; ++g) {
                     float sc = __fmul_rn(acc[g], scale);
@@ -1155,9 +1156,16 @@ __global__ void __launch_bounds__(kThreads) __maxnreg__((RegCap<HD, GP, DT, KP>:
                     vv[0] = DT == DT_BF16 ? bf16_bits_to_f32(raw) : f16_bits_to_f32(raw);
                 }
 #pragma unroll
-                for (int g = 0; g < GS; ++g)
+                for (int g = 0; g < GS; ++g) {
+                    if constexpr (G::DPL % 2 == 0) {
 #pragma unroll
-                    for (int k = 0; k < G::DPL; ++k) o[g][k] = __fmaf_rn(pr_[g], vv[k], o[g][k]);
+                        for (int k = 0; k < G::DPL; k += 2)
+                            fma_x2(o[g][k], o[g][k + 1], pr_[g], pr_[g], vv[k], vv[k + 1]);
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < G::DPL; ++k) o[g][k] = __fmaf_rn(pr_[g], vv[k], o[g][k]);
+                    }
+                }
             
             };
             if (nvalid == kTileRows) {

@@ -352,6 +352,21 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint3
     }
 }
 
+// d0 += a0 * b0 and d1 += a1 * b1 as one fp32x2 fused multiply-add (each
+// half rounded once, as __fmaf_rn): half the FMA instructions of two scalar
+// ones for the CUDA-core dot products.
+__device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1, float b0,
+                                       float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rd, {%0, %1};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // ---------------------------------------------------------------- RoPE
 // One element of a rotated head, rounded as jxai's build rounds apply_rope
 // (src/transformer.cpp:76-138, gcc -O3 -mfma):
