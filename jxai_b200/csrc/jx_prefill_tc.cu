@@ -604,13 +604,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int tile0 = tl.kv_lo + t * BN;
                 const bool masked = tile0 + BN - 1 > hi_all || tile0 < lo_all;
                 float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                if (!capped && !masked) {
+                // plain tiles keep S unscaled: the scale goes into the
+                // exponent's fused multiply-add below, and the row maximum is
+                // scaled once (x -> x * sc_mul is monotone, sc_mul > 0)
+                const bool raw = !capped && !masked;
+                if (raw) {
 #pragma unroll
-                    for (int c = 0; c < SW; ++c) {
-                        const float v = __fmul_rn(__uint_as_float(sr[c]), sc_mul);
-                        sr[c] = __float_as_uint(v);
-                        mx4[c & 3] = fmaxf(mx4[c & 3], v);
-                    }
+                    for (int c = 0; c < SW; ++c)
+                        mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) mx4[i] = __fmul_rn(mx4[i], sc_mul);
                 } else {
 #pragma unroll
                     for (int c = 0; c < SW; ++c) {
@@ -656,12 +659,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 // ex2(-inf) is +0, so masked columns need no test once m is
                 // finite (a row with no attended column yet uses 0).
                 const float mref = m == -INFINITY ? 0.0f : m;
+                // exponent x = s * a_mul - mref * log2(e), two columns per
+                // fp32x2 FMA (s unscaled on plain tiles: a_mul = scale * log2(e))
+                const float a_mul = raw ? sc_mul * kLog2eP : kLog2eP;
+                const float b_add = -mref * kLog2eP;
                 uint32_t hw[SW / 2], lw[SW / 2];
                 float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < SW; c += 2) {
-                    const float p0 = ex2_approx((__uint_as_float(sr[c]) - mref) * kLog2eP);
-                    const float p1 = ex2_approx((__uint_as_float(sr[c + 1]) - mref) * kLog2eP);
+                    float x0 = b_add, x1 = b_add;
+                    fma_x2(x0, x1, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]), a_mul, a_mul);
+                    const float p0 = ex2_approx(x0);
+                    const float p1 = ex2_approx(x1);
                     ls4[(c >> 1) & 3] += p0 + p1;
                     if constexpr (DT == DT_BF16) {
                         // hi: p truncated to bf16 (exact bit mask); lo = p - hi
