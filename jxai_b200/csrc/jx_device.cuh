@@ -367,6 +367,29 @@ __device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1,
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// (d0, d1) += (a0, a1) and (d0, d1) = (a0 - b0, a1 - b1): one packed fp32
+// instruction each, every lane rounded to nearest like a scalar add / sub.
+__device__ __forceinline__ void add_x2(float& d0, float& d1, float a0, float a1) {
+    asm("{\n\t.reg .b64 ra, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rd, {%0, %1};\n\t"
+        "add.rn.f32x2 rd, rd, ra;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "+f"(d0), "+f"(d1)
+        : "f"(a0), "f"(a1));
+}
+
+__device__ __forceinline__ void sub_x2(float& d0, float& d1, float a0, float a1, float b0,
+                                       float b1) {
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\t"
+        "mov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // ---------------------------------------------------------------- RoPE
 // One element of a rotated head, rounded as jxai's build rounds apply_rope
 // (src/transformer.cpp:76-138, gcc -O3 -mfma):

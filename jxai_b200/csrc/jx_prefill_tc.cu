@@ -664,6 +664,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const float a_mul = raw ? sc_mul * kLog2eP : kLog2eP;
                 const float b_add = -mref * kLog2eP;
                 uint32_t hw[SW / 2], lw[SW / 2];
+                // row-sum partials: two pairs, two columns per packed add
                 float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
                 for (int c = 0; c < SW; c += 2) {
@@ -671,7 +672,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     fma_x2(x0, x1, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]), a_mul, a_mul);
                     const float p0 = ex2_approx(x0);
                     const float p1 = ex2_approx(x1);
-                    ls4[(c >> 1) & 3] += p0 + p1;
+                    add_x2(ls4[((c >> 1) & 1) * 2], ls4[((c >> 1) & 1) * 2 + 1], p0, p1);
                     if constexpr (DT == DT_BF16) {
                         // hi: p truncated to bf16 (exact bit mask); lo = p - hi
                         // (exact), rounded to the nearest bf16 by adding half
@@ -681,8 +682,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         const uint32_t b0 = __float_as_uint(p0) & 0xFFFF0000u;
                         const uint32_t b1 = __float_as_uint(p1) & 0xFFFF0000u;
                         hw[c / 2] = __byte_perm(b0, b1, 0x7632);
-                        const uint32_t r0 = __float_as_uint(p0 - __uint_as_float(b0)) + 0x8000u;
-                        const uint32_t r1 = __float_as_uint(p1 - __uint_as_float(b1)) + 0x8000u;
+                        float d0, d1;
+                        sub_x2(d0, d1, p0, p1, __uint_as_float(b0), __uint_as_float(b1));
+                        const uint32_t r0 = __float_as_uint(d0) + 0x8000u;
+                        const uint32_t r1 = __float_as_uint(d1) + 0x8000u;
                         lw[c / 2] = __byte_perm(r0, r1, 0x7632);
                     } else {
                         split_pair<DT>(p0, p1, hw[c / 2], lw[c / 2]);
