@@ -367,6 +367,13 @@ __device__ __forceinline__ void fma_x2(float& d0, float& d1, float a0, float a1,
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// max(a, b, c) in one instruction (a NaN operand is ignored, as by fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // (d0, d1) += (a0, a1) and (d0, d1) = (a0 - b0, a1 - b1): one packed fp32
 // instruction each, every lane rounded to nearest like a scalar add / sub.
 __device__ __forceinline__ void add_x2(float& d0, float& d1, float a0, float a1) {

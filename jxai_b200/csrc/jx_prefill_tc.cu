@@ -610,8 +610,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const bool raw = !capped && !masked;
                 if (raw) {
 #pragma unroll
-                    for (int c = 0; c < SW; ++c)
-                        mx4[c & 3] = fmaxf(mx4[c & 3], __uint_as_float(sr[c]));
+                    for (int c = 0; c < SW; c += 2)
+                        mx4[(c >> 1) & 3] = fmax3(mx4[(c >> 1) & 3], __uint_as_float(sr[c]),
+                                                  __uint_as_float(sr[c + 1]));
 #pragma unroll
                     for (int i = 0; i < 4; ++i) mx4[i] = __fmul_rn(mx4[i], sc_mul);
                 } else {
