@@ -726,7 +726,10 @@ def run_reference(args, rank, world):
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True,
+        # the same key as this config's own arm (a fixed workload is strong scaling)
+        "scaling": "weak" if w.sharding == "replica" else "strong",
+        "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1))", "impl": "reference",
         "config": dict(w.describe(), parallelism="host CPU, OpenMP over heads"),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": orc.max_threads(),
