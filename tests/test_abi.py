@@ -21,6 +21,17 @@ def declared_symbols():
     return sorted(set(re.findall(r"JX_API\s+(?:const\s+)?\w+\*?\s+\**(jx_\w+)\s*\(", text)))
 
 
+def test_cmake_build_compiles_the_same_sources():
+    """CMakeLists.txt (for engines that build with CMake) lists exactly the
+    translation units jxai_b200/build.py compiles, so both libraries export
+    the same entry points."""
+    from jxai_b200 import build
+    with open(os.path.join(ROOT, "CMakeLists.txt")) as fh:
+        text = fh.read()
+    listed = re.search(r"add_library\(jxattn SHARED(.*?)\)", text, re.S).group(1).split()
+    assert sorted(os.path.basename(f) for f in listed) == sorted(build.SOURCES)
+
+
 def test_header_declares_the_binding_list():
     assert declared_symbols() == sorted(_lib.EXPORTS)
 
